@@ -1,0 +1,215 @@
+/*
+ * tqfs.h — C ABI of libtqfsample, the sm_100a token-sampling library.
+ *
+ * This is the boundary a Rust `src/backend/cuda` module binds with
+ * `extern "C"` (see INTEGRATION.md for the binding). Every entry point takes
+ * plain pointers and sizes; no C++ or PyTorch types cross it. Reference
+ * interfaces are cited by path:line inside the TurboQwenFare crate.
+ *
+ * Conventions
+ *   - Every call returns an int status (TQFS_OK == 0). A failed call leaves a
+ *     message retrievable with tqfs_last_error(handle).
+ *   - "_dev" pointers are device memory owned by the caller. The library owns
+ *     only its scratch (grown on demand at call time, never freed per call)
+ *     and the state of a tqfs_sampler.
+ *   - Device calls are stream-ordered and asynchronous unless documented as
+ *     synchronising. One handle per device per host thread.
+ *   - Bad input rows are reported through per-row status words, never by a
+ *     device fault.
+ */
+#ifndef TQFS_H
+#define TQFS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum tqfs_status {
+    TQFS_OK = 0,
+    TQFS_ERR_INVALID_ARG = 1,
+    TQFS_ERR_UNSUPPORTED_DTYPE = 2,
+    TQFS_ERR_CUDA = 3,
+    TQFS_ERR_NCCL = 4,
+    TQFS_ERR_TIMEOUT = 5,
+    TQFS_ERR_UNSUPPORTED = 6,
+    TQFS_ERR_NO_DEVICE = 7,
+    TQFS_ERR_OUT_OF_MEMORY = 8
+};
+
+/* ---- logits element types --------------------------------------------- */
+enum tqfs_dtype {
+    TQFS_DTYPE_F32 = 0,  /* the reference's only type (Vec<f32>)          */
+    TQFS_DTYPE_BF16 = 1  /* widened exactly to f32 before any arithmetic   */
+};
+
+/* ---- per-row status word (out_status_dev) ----------------------------- */
+enum tqfs_row_status {
+    TQFS_ROW_OK = 0,
+    TQFS_ROW_ERR_WINDOW = 1,      /* penalty window beyond the supported size */
+    TQFS_ROW_ERR_UNSUPPORTED = 2, /* row needs a path this build lacks        */
+    TQFS_ROW_ERR_EMPTY = 4        /* vocab == 0: token 0, as the reference    */
+};
+
+/* ---- sampling parameters ---------------------------------------------- */
+#define TQFS_PARAM_HAS_MIN_P 1u /* min_p is Some(..); otherwise None        */
+
+/*
+ * Device mirror of `SamplingParams` (src/runtime/request.rs:46-72). Host-only
+ * fields (seed, stop_sequences, max_output_tokens) are not part of a row:
+ * the seed initialises a tqfs_sampler / the caller's RNG state.
+ *   temperature        0.0 (or -0.0) selects the greedy arm (mod.rs:45-47)
+ *   top_p              >= 1.0 disables (mod.rs:196)
+ *   top_k              Option<u32>: 0 encodes None; Some(0) is also a no-op
+ *   min_p              read only when flags & TQFS_PARAM_HAS_MIN_P
+ *   repeat_penalty     1.0 disables
+ *   frequency_penalty  0.0 disables
+ *   presence_penalty   0.0 disables
+ *   repeat_last_n      usize; UINT64_MAX stands for Ollama's -1
+ * Defaults (request.rs:74-90): {0, 1, 0, 0, 1, 0, 0, 0, 64}.
+ */
+typedef struct tqfs_params {
+    float temperature;
+    float top_p;
+    uint32_t top_k;
+    float min_p;
+    float repeat_penalty;
+    float frequency_penalty;
+    float presence_penalty;
+    uint32_t flags;
+    uint64_t repeat_last_n;
+} tqfs_params; /* 40 bytes, 8-byte aligned */
+
+/* `LogitCandidate` (src/runtime/decode.rs:42-46). */
+typedef struct tqfs_candidate {
+    uint32_t token;
+    float logit;
+} tqfs_candidate;
+
+typedef struct tqfs_handle tqfs_handle;
+typedef struct tqfs_sampler tqfs_sampler;
+
+/* ---- library / handle --------------------------------------------------- */
+int tqfs_version(void);
+const char* tqfs_status_string(int status);
+int tqfs_create(int device, tqfs_handle** out_handle);
+int tqfs_destroy(tqfs_handle* handle);
+const char* tqfs_last_error(const tqfs_handle* handle);
+
+/* Accumulated device time of the library's kernels since the last reset,
+ * measured with CUDA events on the launching stream when timing is enabled.
+ * kernel_ms[i] and launches[i] are filled for i < n (order: stream,
+ * finalize-in-stream share is included in stream; general; mtp). Test and
+ * benchmark instrumentation only. */
+int tqfs_set_timing(tqfs_handle* handle, int enabled);
+int tqfs_get_timing(tqfs_handle* handle, int n, float* kernel_ms, int64_t* launches);
+
+/* ---- host RNG helpers (no device work) ---------------------------------- */
+/* `Xoshiro256PlusPlus::from_seed` (src/sampling/mod.rs:283-295). */
+void tqfs_xoshiro_from_seed(uint64_t seed, uint64_t state_out[4]);
+/* `Xoshiro256PlusPlus::next_u64` (src/sampling/mod.rs:311-324). */
+uint64_t tqfs_xoshiro_next_u64(uint64_t state[4]);
+/* `next_f32` (src/sampling/mod.rs:328-330): (next_u64 >> 40) / 2^24. */
+float tqfs_xoshiro_next_f32(uint64_t state[4]);
+
+/* ---- batched device sampling -------------------------------------------- */
+/*
+ * Batched `Sampler::select` over `rows` logits rows (src/sampling/mod.rs:
+ * 68-73, 84-106). Replaces, per row, the pair at src/model/qwen36/
+ * runtime.rs:442-443 (top_logit_candidates + sampler.select).
+ *
+ *   logits_dev      rows x ld elements of `dtype`; row r starts at r*ld
+ *   vocab           V, number of logits per row (>= 0)
+ *   ld              row stride in elements (>= vocab)
+ *   hist_dev        concatenated per-row token histories (reference: &[u32];
+ *                   int32 here, values >= vocab or < 0 never match a token,
+ *                   as at src/sampling/mod.rs:135-138)
+ *   hist_off_dev    rows+1 offsets into hist_dev (int64); NULL = no history
+ *   params_dev      rows x tqfs_params
+ *   uniforms_dev    rows floats in [0,1) consumed by the draw, or NULL to
+ *                   draw from rng_state_dev
+ *   rng_state_dev   rows x 4 uint64 xoshiro256++ states, advanced only when
+ *                   the draw consumes a uniform (mod.rs:235-238); may be NULL
+ *                   when uniforms_dev is given
+ *   out_token_dev   rows int32 sampled token ids (greedy rows: the
+ *                   top_logit_candidates argmax of the raw logits)
+ *   out_top4_dev    rows x 4 tqfs_candidate diagnostics (decode.rs:48-64) of
+ *                   the raw logits, or NULL
+ *   out_probs_dev   rows x ld float: post-filter probability of every token
+ *                   (0 where filtered out), or NULL. Debug output.
+ *   out_status_dev  rows int32 tqfs_row_status, or NULL
+ *   stream          cudaStream_t (NULL = legacy default stream)
+ */
+int tqfs_sample(tqfs_handle* handle, const void* logits_dev, int dtype, int rows,
+                int vocab, int64_t ld, const int32_t* hist_dev,
+                const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                const float* uniforms_dev, uint64_t* rng_state_dev,
+                int32_t* out_token_dev, tqfs_candidate* out_top4_dev,
+                float* out_probs_dev, int32_t* out_status_dev, void* stream);
+
+/*
+ * Host-buffer form of tqfs_sample (same argument meaning, host pointers;
+ * pinned memory gives full copy bandwidth). Copies inputs to library-owned
+ * device buffers with one cudaMemcpyAsync per buffer, samples, copies the
+ * tokens back and synchronises the stream. rng_state_host (may be NULL when
+ * uniforms_host is given) is read before and written back after the call.
+ */
+int tqfs_sample_host(tqfs_handle* handle, const void* logits_host, int dtype, int rows,
+                     int vocab, int64_t ld, const int32_t* hist_host,
+                     const int64_t* hist_off_host, const tqfs_params* params_host,
+                     const float* uniforms_host, uint64_t* rng_state_host,
+                     int32_t* out_token_host, void* stream);
+
+/*
+ * `top_logit_candidates` (src/runtime/decode.rs:48-64) over rows of raw
+ * logits: top 4 by strict '>', lowest index first on ties, NaN never ranks,
+ * unfilled slots stay {0, -inf}.
+ */
+int tqfs_top_logit_candidates(tqfs_handle* handle, const void* logits_dev, int dtype,
+                              int rows, int vocab, int64_t ld,
+                              tqfs_candidate* out_top4_dev, void* stream);
+
+/*
+ * Penalised logits `apply_penalties` (src/sampling/mod.rs:114-148) written as
+ * f32 rows to out_dev (rows x ld; columns >= vocab untouched). Each row is
+ * penalised with its own params and history window. An inspection and test
+ * entry point: the sampling kernels apply the same penalties inline. Its
+ * cost grows with the square of the window length.
+ */
+int tqfs_apply_penalties(tqfs_handle* handle, const void* logits_dev, int dtype, int rows,
+                         int vocab, int64_t ld, const int32_t* hist_dev,
+                         const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                         float* out_dev, void* stream);
+
+/* ---- drop-in Sampler (host pointers; synchronising) ---------------------- */
+/*
+ * `Sampler::new(&SamplingParams)` (src/sampling/mod.rs:45-53): greedy iff
+ * temperature == 0.0; otherwise seeds xoshiro256++ from `seed` (has_seed=1)
+ * or from the wall clock as mod.rs:302-309 does.
+ */
+int tqfs_sampler_new(tqfs_handle* handle, const tqfs_params* params, int has_seed,
+                     uint64_t seed, tqfs_sampler** out_sampler);
+/* `Sampler::is_greedy` (mod.rs:55-57): 1 greedy, 0 stochastic. */
+int tqfs_sampler_is_greedy(const tqfs_sampler* sampler);
+/*
+ * `Sampler::select(&mut self, logits, history, greedy_token)`
+ * (mod.rs:68-73). The greedy arm returns greedy_token without touching the
+ * logits. The stochastic arm copies one host row (vocab f32) and the history
+ * to the device, samples, and returns the token (one H2D copy per call is the
+ * documented cost of this single-row shim).
+ */
+int tqfs_sampler_select(tqfs_sampler* sampler, const float* logits_host, int64_t vocab,
+                        const uint32_t* history_host, int64_t history_len,
+                        uint32_t greedy_token, uint32_t* out_token);
+/* Copies the sampler's xoshiro state to state_out (checkpoint). */
+int tqfs_sampler_get_state(const tqfs_sampler* sampler, uint64_t state_out[4]);
+int tqfs_sampler_free(tqfs_sampler* sampler);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TQFS_H */

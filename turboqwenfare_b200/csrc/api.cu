@@ -1,0 +1,569 @@
+// C ABI of libtqfsample: handle, scratch, batched sampling entry points, the
+// drop-in single-row Sampler and host RNG helpers. See include/tqfs.h.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+constexpr int kVersion = 1;
+
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t reserve(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        size_t cap = want < 4096 ? 4096 : want + want / 4;
+        cudaError_t e = cudaMalloc(&ptr, cap);
+        if (e != cudaSuccess) return e;
+        bytes = cap;
+        return cudaSuccess;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+struct TimedLaunch {
+    cudaEvent_t start;
+    cudaEvent_t stop;
+    int kind;
+};
+
+}  // namespace
+
+struct tqfs_handle {
+    int device = 0;
+    std::string error;
+    DeviceBuffer scratch;      // candidate lists, counts, greedy lists
+    DeviceBuffer tickets;      // per-row tickets, kept zero between launches
+    size_t ticket_rows = 0;
+    // staging for the host-buffer entry points
+    DeviceBuffer h_logits, h_hist, h_off, h_params, h_unif, h_rng, h_tok;
+    cudaStream_t own_stream = nullptr;
+    bool timing = false;
+    std::vector<TimedLaunch> pending;
+    std::vector<cudaEvent_t> free_events;
+    double kernel_ms[4] = {0, 0, 0, 0};
+    long long launches[4] = {0, 0, 0, 0};
+};
+
+struct tqfs_sampler {
+    tqfs_handle* handle = nullptr;
+    tqfs_params params{};
+    bool greedy = true;
+    uint64_t state[4] = {0, 0, 0, 0};
+    DeviceBuffer logits, hist, misc;  // misc: params | off[2] | rng[4] | token | status
+};
+
+namespace {
+
+int fail(tqfs_handle* h, int status, const char* fmt, ...) {
+    if (h) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        h->error = buf;
+    }
+    return status;
+}
+
+int cuda_fail(tqfs_handle* h, cudaError_t e, const char* what) {
+    return fail(h, e == cudaErrorMemoryAllocation ? TQFS_ERR_OUT_OF_MEMORY : TQFS_ERR_CUDA,
+                "%s: %s", what, cudaGetErrorString(e));
+}
+
+cudaEvent_t take_event(tqfs_handle* h) {
+    if (!h->free_events.empty()) {
+        cudaEvent_t e = h->free_events.back();
+        h->free_events.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void drain_timing(tqfs_handle* h) {
+    for (auto& t : h->pending) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(t.stop) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, t.start, t.stop) == cudaSuccess) {
+            h->kernel_ms[t.kind] += ms;
+            h->launches[t.kind] += 1;
+        }
+        h->free_events.push_back(t.start);
+        h->free_events.push_back(t.stop);
+    }
+    h->pending.clear();
+}
+
+struct TimingScope {
+    tqfs_handle* h;
+    cudaStream_t s;
+    int kind;
+    cudaEvent_t start = nullptr;
+    TimingScope(tqfs_handle* h_, cudaStream_t s_, int kind_) : h(h_), s(s_), kind(kind_) {
+        if (h->timing) {
+            if (h->pending.size() > 8192) drain_timing(h);
+            start = take_event(h);
+            cudaEventRecord(start, s);
+        }
+    }
+    ~TimingScope() {
+        if (start) {
+            cudaEvent_t stop = take_event(h);
+            cudaEventRecord(stop, s);
+            h->pending.push_back(TimedLaunch{start, stop, kind});
+        }
+    }
+};
+
+int ensure_current(tqfs_handle* h) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != h->device) {
+        cudaError_t e = cudaSetDevice(h->device);
+        if (e != cudaSuccess) return cuda_fail(h, e, "cudaSetDevice");
+    }
+    return TQFS_OK;
+}
+
+// Scratch for the stream kernel; tickets are zeroed when (re)allocated and
+// the kernel leaves them zero.
+int ensure_scratch(tqfs_handle* h, int rows, int slices, tqfs::SampleArgs& a) {
+    const size_t ls = static_cast<size_t>(rows) * slices;
+    const size_t cand = ls * tqfs::kMaxK * 8;
+    const size_t cn = (ls * 4 + 255) & ~static_cast<size_t>(255);
+    const size_t t4 = ls * 4 * 8;
+    cudaError_t e = h->scratch.reserve(cand + cn + t4);
+    if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
+    if (static_cast<size_t>(rows) > h->ticket_rows) {
+        e = h->tickets.reserve(static_cast<size_t>(rows) * 4);
+        if (e != cudaSuccess) return cuda_fail(h, e, "ticket allocation");
+        e = cudaMemset(h->tickets.ptr, 0, h->tickets.bytes);
+        if (e != cudaSuccess) return cuda_fail(h, e, "ticket reset");
+        h->ticket_rows = h->tickets.bytes / 4;
+    }
+    unsigned char* base = static_cast<unsigned char*>(h->scratch.ptr);
+    a.cand = reinterpret_cast<unsigned long long*>(base);
+    a.cand_n = reinterpret_cast<int*>(base + cand);
+    a.top4 = reinterpret_cast<unsigned long long*>(base + cand + cn);
+    a.ticket = static_cast<unsigned int*>(h->tickets.ptr);
+    return TQFS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
+    if (a.rows == 0) return TQFS_OK;
+    if (a.vocab == 0) {
+        cudaError_t e = tqfs::launch_fill_empty(a.rows, a.out_token, a.out_status, a.out_top4, s);
+        return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "launch");
+    }
+    const tqfs::Plan plan = tqfs::plan_stream(a.vocab);
+    if (plan.slices > 64) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
+    int st = ensure_scratch(h, a.rows, plan.slices, a);
+    if (st != TQFS_OK) return st;
+    a.slices = plan.slices;
+    a.slice_len = plan.slice_len;
+    const size_t esz = a.dtype == TQFS_DTYPE_F32 ? 4 : 2;
+    a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
+    cudaError_t e;
+    {
+        TimingScope ts(h, s, 0);
+        e = tqfs::launch_stream(a, plan, s);
+    }
+    if (e != cudaSuccess) {
+        cudaMemsetAsync(h->tickets.ptr, 0, h->tickets.bytes, s);
+        return cuda_fail(h, e, "stream kernel launch");
+    }
+    return TQFS_OK;
+}
+
+int check_common(tqfs_handle* h, const void* logits, int dtype, int rows, int vocab,
+                 int64_t ld) {
+    if (!h) return TQFS_ERR_INVALID_ARG;
+    if (dtype != TQFS_DTYPE_F32 && dtype != TQFS_DTYPE_BF16)
+        return fail(h, TQFS_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+    if (rows < 0 || vocab < 0 || ld < vocab)
+        return fail(h, TQFS_ERR_INVALID_ARG, "rows=%d vocab=%d ld=%lld", rows, vocab,
+                    static_cast<long long>(ld));
+    if (rows > 0 && vocab > 0 && !logits) return fail(h, TQFS_ERR_INVALID_ARG, "logits is NULL");
+    return TQFS_OK;
+}
+
+// Host xoshiro256++ (src/sampling/mod.rs:283-330).
+uint64_t host_rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+}  // namespace
+
+extern "C" {
+
+int tqfs_version(void) { return kVersion; }
+
+const char* tqfs_status_string(int status) {
+    switch (status) {
+        case TQFS_OK: return "ok";
+        case TQFS_ERR_INVALID_ARG: return "invalid argument";
+        case TQFS_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+        case TQFS_ERR_CUDA: return "CUDA error";
+        case TQFS_ERR_NCCL: return "NCCL error";
+        case TQFS_ERR_TIMEOUT: return "timeout";
+        case TQFS_ERR_UNSUPPORTED: return "unsupported";
+        case TQFS_ERR_NO_DEVICE: return "no CUDA device";
+        case TQFS_ERR_OUT_OF_MEMORY: return "out of device memory";
+        default: return "unknown status";
+    }
+}
+
+int tqfs_create(int device, tqfs_handle** out_handle) {
+    if (!out_handle) return TQFS_ERR_INVALID_ARG;
+    *out_handle = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return TQFS_ERR_NO_DEVICE;
+    if (device < 0 || device >= count) return TQFS_ERR_INVALID_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return TQFS_ERR_CUDA;
+    tqfs_handle* h = new (std::nothrow) tqfs_handle();
+    if (!h) return TQFS_ERR_OUT_OF_MEMORY;
+    h->device = device;
+    if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete h;
+        return TQFS_ERR_CUDA;
+    }
+    *out_handle = h;
+    return TQFS_OK;
+}
+
+int tqfs_destroy(tqfs_handle* h) {
+    if (!h) return TQFS_OK;
+    cudaSetDevice(h->device);
+    cudaDeviceSynchronize();
+    drain_timing(h);
+    for (cudaEvent_t e : h->free_events) cudaEventDestroy(e);
+    h->scratch.release();
+    h->tickets.release();
+    h->h_logits.release();
+    h->h_hist.release();
+    h->h_off.release();
+    h->h_params.release();
+    h->h_unif.release();
+    h->h_rng.release();
+    h->h_tok.release();
+    if (h->own_stream) cudaStreamDestroy(h->own_stream);
+    delete h;
+    return TQFS_OK;
+}
+
+const char* tqfs_last_error(const tqfs_handle* h) { return h ? h->error.c_str() : "null handle"; }
+
+int tqfs_set_timing(tqfs_handle* h, int enabled) {
+    if (!h) return TQFS_ERR_INVALID_ARG;
+    drain_timing(h);
+    h->timing = enabled != 0;
+    for (int i = 0; i < 4; ++i) {
+        h->kernel_ms[i] = 0.0;
+        h->launches[i] = 0;
+    }
+    return TQFS_OK;
+}
+
+int tqfs_get_timing(tqfs_handle* h, int n, float* kernel_ms, int64_t* launches) {
+    if (!h || n < 0) return TQFS_ERR_INVALID_ARG;
+    drain_timing(h);
+    for (int i = 0; i < n && i < 4; ++i) {
+        if (kernel_ms) kernel_ms[i] = static_cast<float>(h->kernel_ms[i]);
+        if (launches) launches[i] = h->launches[i];
+    }
+    return TQFS_OK;
+}
+
+void tqfs_xoshiro_from_seed(uint64_t seed, uint64_t s[4]) {
+    uint64_t z = seed;
+    for (int i = 0; i < 4; ++i) {
+        z += 0x9E3779B97F4A7C15ull;
+        uint64_t x = z;
+        x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+        x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+        s[i] = x ^ (x >> 31);
+    }
+}
+
+uint64_t tqfs_xoshiro_next_u64(uint64_t s[4]) {
+    const uint64_t result = host_rotl(s[0] + s[3], 23) + s[0];
+    const uint64_t t = s[1] << 17;
+    s[2] ^= s[0];
+    s[3] ^= s[1];
+    s[1] ^= s[2];
+    s[0] ^= s[3];
+    s[2] ^= t;
+    s[3] = host_rotl(s[3], 45);
+    return result;
+}
+
+float tqfs_xoshiro_next_f32(uint64_t s[4]) {
+    return static_cast<float>(tqfs_xoshiro_next_u64(s) >> 40) / static_cast<float>(1u << 24);
+}
+
+int tqfs_sample(tqfs_handle* h, const void* logits_dev, int dtype, int rows, int vocab,
+                int64_t ld, const int32_t* hist_dev, const int64_t* hist_off_dev,
+                const tqfs_params* params_dev, const float* uniforms_dev,
+                uint64_t* rng_state_dev, int32_t* out_token_dev, tqfs_candidate* out_top4_dev,
+                float* out_probs_dev, int32_t* out_status_dev, void* stream) {
+    int st = check_common(h, logits_dev, dtype, rows, vocab, ld);
+    if (st != TQFS_OK) return st;
+    if (rows > 0 && !params_dev) return fail(h, TQFS_ERR_INVALID_ARG, "params is NULL");
+    if (rows > 0 && !uniforms_dev && !rng_state_dev)
+        return fail(h, TQFS_ERR_INVALID_ARG, "need uniforms or rng_state");
+    if (hist_off_dev && !hist_dev) return fail(h, TQFS_ERR_INVALID_ARG, "history is NULL");
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    tqfs::SampleArgs a{};
+    a.logits = logits_dev;
+    a.dtype = dtype;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.ld = ld;
+    a.hist = hist_dev;
+    a.hist_off = hist_off_dev;
+    a.params = params_dev;
+    a.uniforms = uniforms_dev;
+    a.rng_state = rng_state_dev;
+    a.out_token = out_token_dev;
+    a.out_top4 = out_top4_dev;
+    a.out_probs = out_probs_dev;
+    a.out_status = out_status_dev;
+    a.top4_only = 0;
+    return run_sample(h, a, static_cast<cudaStream_t>(stream));
+}
+
+int tqfs_top_logit_candidates(tqfs_handle* h, const void* logits_dev, int dtype, int rows,
+                              int vocab, int64_t ld, tqfs_candidate* out_top4_dev,
+                              void* stream) {
+    int st = check_common(h, logits_dev, dtype, rows, vocab, ld);
+    if (st != TQFS_OK) return st;
+    if (rows > 0 && !out_top4_dev) return fail(h, TQFS_ERR_INVALID_ARG, "out_top4 is NULL");
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    tqfs::SampleArgs a{};
+    a.logits = logits_dev;
+    a.dtype = dtype;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.ld = ld;
+    a.out_top4 = out_top4_dev;
+    a.top4_only = 1;
+    return run_sample(h, a, static_cast<cudaStream_t>(stream));
+}
+
+int tqfs_sample_host(tqfs_handle* h, const void* logits_host, int dtype, int rows, int vocab,
+                     int64_t ld, const int32_t* hist_host, const int64_t* hist_off_host,
+                     const tqfs_params* params_host, const float* uniforms_host,
+                     uint64_t* rng_state_host, int32_t* out_token_host, void* stream) {
+    int st = check_common(h, logits_host, dtype, rows, vocab, ld);
+    if (st != TQFS_OK) return st;
+    if (rows == 0) return TQFS_OK;
+    if (!params_host || !out_token_host) return fail(h, TQFS_ERR_INVALID_ARG, "NULL argument");
+    if (!uniforms_host && !rng_state_host)
+        return fail(h, TQFS_ERR_INVALID_ARG, "need uniforms or rng_state");
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->own_stream;
+    const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
+    const size_t lbytes = static_cast<size_t>(rows) * static_cast<size_t>(ld) * esz;
+    int64_t hist_n = 0;
+    if (hist_off_host) {
+        if (!hist_host) return fail(h, TQFS_ERR_INVALID_ARG, "history is NULL");
+        hist_n = hist_off_host[rows];
+    }
+    cudaError_t e;
+    if ((e = h->h_logits.reserve(lbytes)) != cudaSuccess ||
+        (e = h->h_params.reserve(sizeof(tqfs_params) * rows)) != cudaSuccess ||
+        (e = h->h_tok.reserve(sizeof(int32_t) * rows)) != cudaSuccess)
+        return cuda_fail(h, e, "staging allocation");
+    if (hist_off_host) {
+        if ((e = h->h_hist.reserve(sizeof(int32_t) * (hist_n > 0 ? hist_n : 1))) != cudaSuccess ||
+            (e = h->h_off.reserve(sizeof(int64_t) * (rows + 1))) != cudaSuccess)
+            return cuda_fail(h, e, "staging allocation");
+    }
+    if (uniforms_host && (e = h->h_unif.reserve(sizeof(float) * rows)) != cudaSuccess)
+        return cuda_fail(h, e, "staging allocation");
+    if (!uniforms_host && (e = h->h_rng.reserve(sizeof(uint64_t) * 4 * rows)) != cudaSuccess)
+        return cuda_fail(h, e, "staging allocation");
+    // One cudaMemcpyAsync per input buffer.
+    e = cudaMemcpyAsync(h->h_logits.ptr, logits_host, lbytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(h->h_params.ptr, params_host, sizeof(tqfs_params) * rows,
+                            cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && hist_off_host) {
+        if (hist_n > 0)
+            e = cudaMemcpyAsync(h->h_hist.ptr, hist_host, sizeof(int32_t) * hist_n,
+                                cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(h->h_off.ptr, hist_off_host, sizeof(int64_t) * (rows + 1),
+                                cudaMemcpyHostToDevice, s);
+    }
+    if (e == cudaSuccess && uniforms_host)
+        e = cudaMemcpyAsync(h->h_unif.ptr, uniforms_host, sizeof(float) * rows,
+                            cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && !uniforms_host)
+        e = cudaMemcpyAsync(h->h_rng.ptr, rng_state_host, sizeof(uint64_t) * 4 * rows,
+                            cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "host-to-device copy");
+    tqfs::SampleArgs a{};
+    a.logits = h->h_logits.ptr;
+    a.dtype = dtype;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.ld = ld;
+    a.hist = hist_off_host ? static_cast<const int32_t*>(h->h_hist.ptr) : nullptr;
+    a.hist_off = hist_off_host ? static_cast<const int64_t*>(h->h_off.ptr) : nullptr;
+    a.params = static_cast<const tqfs_params*>(h->h_params.ptr);
+    a.uniforms = uniforms_host ? static_cast<const float*>(h->h_unif.ptr) : nullptr;
+    a.rng_state = uniforms_host ? nullptr : static_cast<uint64_t*>(h->h_rng.ptr);
+    a.out_token = static_cast<int32_t*>(h->h_tok.ptr);
+    st = run_sample(h, a, s);
+    if (st != TQFS_OK) return st;
+    e = cudaMemcpyAsync(out_token_host, h->h_tok.ptr, sizeof(int32_t) * rows,
+                        cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && !uniforms_host)
+        e = cudaMemcpyAsync(rng_state_host, h->h_rng.ptr, sizeof(uint64_t) * 4 * rows,
+                            cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "device-to-host copy");
+    return TQFS_OK;
+}
+
+int tqfs_apply_penalties(tqfs_handle* h, const void* logits_dev, int dtype, int rows, int vocab,
+                         int64_t ld, const int32_t* hist_dev, const int64_t* hist_off_dev,
+                         const tqfs_params* params_dev, float* out_dev, void* stream) {
+    int st = check_common(h, logits_dev, dtype, rows, vocab, ld);
+    if (st != TQFS_OK) return st;
+    if (rows > 0 && (!params_dev || !out_dev)) return fail(h, TQFS_ERR_INVALID_ARG, "NULL argument");
+    if (hist_off_dev && !hist_dev) return fail(h, TQFS_ERR_INVALID_ARG, "history is NULL");
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    cudaError_t e = tqfs::launch_penalties(logits_dev, dtype, rows, vocab, ld, hist_dev, hist_off_dev,
+                                           params_dev, out_dev, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "penalties launch");
+}
+
+// ---- drop-in Sampler -------------------------------------------------------
+
+int tqfs_sampler_new(tqfs_handle* h, const tqfs_params* params, int has_seed, uint64_t seed,
+                     tqfs_sampler** out) {
+    if (!h || !params || !out) return TQFS_ERR_INVALID_ARG;
+    *out = nullptr;
+    tqfs_sampler* s = new (std::nothrow) tqfs_sampler();
+    if (!s) return TQFS_ERR_OUT_OF_MEMORY;
+    s->handle = h;
+    s->params = *params;
+    s->greedy = params->temperature == 0.0f;
+    if (!s->greedy) {
+        uint64_t sd = seed;
+        if (!has_seed) {  // src/sampling/mod.rs:302-309: wall clock nanoseconds
+            const auto ns = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                std::chrono::system_clock::now().time_since_epoch())
+                                .count();
+            sd = ns > 0 ? static_cast<uint64_t>(ns) : 0x5DEECE66D1CE1234ull;
+        }
+        tqfs_xoshiro_from_seed(sd, s->state);
+    }
+    *out = s;
+    return TQFS_OK;
+}
+
+int tqfs_sampler_is_greedy(const tqfs_sampler* s) { return s && s->greedy ? 1 : 0; }
+
+int tqfs_sampler_get_state(const tqfs_sampler* s, uint64_t state_out[4]) {
+    if (!s || !state_out) return TQFS_ERR_INVALID_ARG;
+    std::memcpy(state_out, s->state, sizeof(s->state));
+    return TQFS_OK;
+}
+
+int tqfs_sampler_select(tqfs_sampler* s, const float* logits_host, int64_t vocab,
+                        const uint32_t* history_host, int64_t history_len,
+                        uint32_t greedy_token, uint32_t* out_token) {
+    if (!s || !out_token) return TQFS_ERR_INVALID_ARG;
+    if (s->greedy) {  // src/sampling/mod.rs:70: the caller's argmax, verbatim
+        *out_token = greedy_token;
+        return TQFS_OK;
+    }
+    tqfs_handle* h = s->handle;
+    if (vocab < 0 || vocab > 0x7FFFFFFF || history_len < 0 || (vocab > 0 && !logits_host) ||
+        (history_len > 0 && !history_host))
+        return fail(h, TQFS_ERR_INVALID_ARG, "bad select arguments");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    cudaStream_t cs = h->own_stream;
+    cudaError_t e;
+    const size_t misc = sizeof(tqfs_params) + 2 * sizeof(int64_t) + 4 * sizeof(uint64_t) + 16;
+    if ((e = s->logits.reserve(static_cast<size_t>(vocab > 0 ? vocab : 1) * 4)) != cudaSuccess ||
+        (e = s->hist.reserve(static_cast<size_t>(history_len > 0 ? history_len : 1) * 4)) !=
+            cudaSuccess ||
+        (e = s->misc.reserve(misc)) != cudaSuccess)
+        return cuda_fail(h, e, "sampler allocation");
+    unsigned char host_misc[sizeof(tqfs_params) + 2 * sizeof(int64_t) + 4 * sizeof(uint64_t)];
+    std::memcpy(host_misc, &s->params, sizeof(tqfs_params));
+    const int64_t off[2] = {0, history_len};
+    std::memcpy(host_misc + sizeof(tqfs_params), off, sizeof(off));
+    std::memcpy(host_misc + sizeof(tqfs_params) + sizeof(off), s->state, sizeof(s->state));
+    unsigned char* dm = static_cast<unsigned char*>(s->misc.ptr);
+    e = cudaMemcpyAsync(dm, host_misc, sizeof(host_misc), cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess && vocab > 0)
+        e = cudaMemcpyAsync(s->logits.ptr, logits_host, static_cast<size_t>(vocab) * 4,
+                            cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess && history_len > 0)
+        e = cudaMemcpyAsync(s->hist.ptr, history_host, static_cast<size_t>(history_len) * 4,
+                            cudaMemcpyHostToDevice, cs);
+    if (e != cudaSuccess) return cuda_fail(h, e, "select copy");
+    tqfs::SampleArgs a{};
+    a.logits = s->logits.ptr;
+    a.dtype = TQFS_DTYPE_F32;
+    a.rows = 1;
+    a.vocab = static_cast<int>(vocab);
+    a.ld = vocab > 0 ? vocab : 1;
+    a.hist = static_cast<const int32_t*>(s->hist.ptr);
+    a.hist_off = reinterpret_cast<const int64_t*>(dm + sizeof(tqfs_params));
+    a.params = reinterpret_cast<const tqfs_params*>(dm);
+    a.rng_state = reinterpret_cast<uint64_t*>(dm + sizeof(tqfs_params) + sizeof(off));
+    int32_t* dtok = reinterpret_cast<int32_t*>(dm + sizeof(host_misc));
+    a.out_token = dtok;
+    a.out_status = dtok + 1;
+    st = run_sample(h, a, cs);
+    if (st != TQFS_OK) return st;
+    int32_t res[2] = {0, 0};
+    e = cudaMemcpyAsync(res, dtok, sizeof(res), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(s->state, a.rng_state, sizeof(s->state), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
+    if (e != cudaSuccess) return cuda_fail(h, e, "select result copy");
+    if (res[1] != TQFS_ROW_OK && res[1] != TQFS_ROW_ERR_EMPTY)
+        return fail(h, TQFS_ERR_UNSUPPORTED, "row status %d", res[1]);
+    *out_token = static_cast<uint32_t>(res[0]);
+    return TQFS_OK;
+}
+
+int tqfs_sampler_free(tqfs_sampler* s) {
+    if (!s) return TQFS_OK;
+    if (s->handle) cudaSetDevice(s->handle->device);
+    s->logits.release();
+    s->hist.release();
+    s->misc.release();
+    delete s;
+    return TQFS_OK;
+}
+
+}  // extern "C"

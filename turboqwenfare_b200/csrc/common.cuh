@@ -1,0 +1,140 @@
+// Device helpers shared by the sampling kernels (sm_100a).
+//
+// Ordering keys. The reference orders candidates with compare_desc
+// (src/sampling/mod.rs:258-266: descending, NaN last, -0.0 == +0.0) and breaks
+// ties by ascending token id (mod.rs:188; the same rule is this library's
+// pinned top-k tie policy). Both are folded into one unsigned 64-bit key:
+//   key = (order32(value) << 32) | (0xFFFFFFFF - token)
+// so "larger key" == "earlier in the reference's order" and every key of a
+// row is distinct. order32 maps NaN to 0 (below -inf) and -0.0 to +0.0.
+//
+// Arithmetic. Every floating-point step the reference performs as a separate
+// Rust operation is written with an explicit round-to-nearest intrinsic
+// (__fadd_rn, __fmul_rn, __fdiv_rn, ...) so nvcc cannot contract it into an
+// FMA; the library is built without --use_fast_math.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/tqfs.h"
+
+namespace tqfs {
+
+constexpr int kThreads = 256;        // threads per CTA of the stream kernel
+constexpr int kWarps = kThreads / 32;
+constexpr int kElemsPerThread = 40;  // logits held in registers per thread
+constexpr int kMaxSliceLen = kThreads * kElemsPerThread;  // 10,240 ids
+constexpr int kMaxK = 256;           // top_k handled by the stream kernel
+constexpr int kCandCap = 1024;       // per-CTA candidate list capacity
+constexpr int kRecountCap = 64;      // saturated-count ids per CTA
+
+__device__ __forceinline__ uint32_t order32(float v) {
+    uint32_t b = __float_as_uint(v);
+    if (v != v) return 0u;            // NaN sorts after everything
+    if (v == 0.0f) b = 0u;            // -0.0 == +0.0
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float from_order32(uint32_t k) {
+    if (k == 0u) return __uint_as_float(0x7FC00000u);  // NaN
+    const uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(b);
+}
+
+__device__ __forceinline__ uint64_t make_key(uint32_t ord, uint32_t token) {
+    return (static_cast<uint64_t>(ord) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - token);
+}
+__device__ __forceinline__ uint32_t key_token(uint64_t key) {
+    return 0xFFFFFFFFu - static_cast<uint32_t>(key);
+}
+__device__ __forceinline__ float key_value(uint64_t key) {
+    return from_order32(static_cast<uint32_t>(key >> 32));
+}
+
+// top_logit_candidates ranks by strict '>' against an initial -inf
+// (src/runtime/decode.rs:48-64): neither NaN nor -inf can ever enter it.
+// 0 marks "no candidate".
+__device__ __forceinline__ uint64_t greedy_key(float v, uint32_t token) {
+    if (!(v > -INFINITY)) return 0ull;
+    return make_key(order32(v), token);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h16) {
+    return __uint_as_float(h16 << 16);
+}
+
+// apply_penalties body (src/sampling/mod.rs:139-146) for one repeated token.
+__device__ __forceinline__ float penalise(float v, uint32_t count, float repeat,
+                                          float frequency, float presence) {
+    if (repeat != 1.0f) v = (v > 0.0f) ? __fdiv_rn(v, repeat) : __fmul_rn(v, repeat);
+    float t = __fmul_rn(frequency, __uint2float_rn(count));
+    t = __fadd_rn(t, presence);
+    return __fsub_rn(v, t);
+}
+
+// exp of an f32 argument, rounded once to f32 from a double-precision
+// evaluation. This is the correctly rounded result in all but vanishingly
+// rare cases; glibc's expf (what Rust's f32::exp calls on Linux) returns the
+// same value except for about 9 in 100,000 arguments, where the two differ
+// by one ulp (measured exhaustively over [-104, 88.7] on the build host).
+__device__ __forceinline__ float exp_f32(float x) {
+    return __double2float_rn(exp(static_cast<double>(x)));
+}
+
+// xoshiro256++ (src/sampling/mod.rs:311-330).
+__device__ __forceinline__ uint64_t rotl64(uint64_t x, int k) {
+    return (x << k) | (x >> (64 - k));
+}
+__device__ __forceinline__ uint64_t xoshiro_next(uint64_t s[4]) {
+    const uint64_t result = rotl64(s[0] + s[3], 23) + s[0];
+    const uint64_t t = s[1] << 17;
+    s[2] ^= s[0];
+    s[3] ^= s[1];
+    s[1] ^= s[2];
+    s[0] ^= s[3];
+    s[2] ^= t;
+    s[3] = rotl64(s[3], 45);
+    return result;
+}
+__device__ __forceinline__ float xoshiro_next_f32(uint64_t s[4]) {
+    return __fdiv_rn(__uint2float_rn(static_cast<uint32_t>(xoshiro_next(s) >> 40)),
+                     16777216.0f);
+}
+
+__device__ __forceinline__ uint64_t umax64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+__device__ __forceinline__ uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+// Descending bitonic sort of one u64 per lane across a full warp.
+__device__ __forceinline__ uint64_t warp_sort_desc(uint64_t x, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, x, stride);
+            const bool desc = (lane & size) == 0;
+            const bool lower = (lane & stride) == 0;
+            x = (lower == desc) ? umax64(x, o) : umin64(x, o);
+        }
+    }
+    return x;
+}
+
+__device__ __forceinline__ uint64_t warp_max64(uint64_t x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = umax64(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+    return x;
+}
+
+__device__ __forceinline__ int warp_sum(int x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, o);
+    return x;
+}
+
+// Streaming 16-byte load: read once, evict first.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+
+}  // namespace tqfs
