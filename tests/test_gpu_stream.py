@@ -98,7 +98,7 @@ def test_small_vocab_edges(cuda_device, vocab):
     ps = []
     for r in range(rows):
         k = [1, 2, 20, 255, 256, vocab - 1][r % 6]
-        k = max(1, min(k, vocab - 1)) if vocab > 1 else 0
+        k = max(1, min(k, vocab - 1, 256)) if vocab > 1 else 0
         T = [0.0, 0.3, 1.0, 1.9][r % 4]
         top_p = [1.0, 0.9, 0.5, 0.0][(r // 2) % 4]
         mp = [None, 0.05, 0.5][(r // 3) % 3]

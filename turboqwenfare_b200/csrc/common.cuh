@@ -27,7 +27,7 @@ constexpr int kElemsPerThread = 40;  // logits held in registers per thread
 constexpr int kMaxSliceLen = kThreads * kElemsPerThread;  // 10,240 ids
 constexpr int kMaxK = 256;           // top_k handled by the stream kernel
 constexpr int kCandCap = 1024;       // per-CTA candidate list capacity
-constexpr int kRecountCap = 64;      // saturated-count ids per CTA
+constexpr int kFirstsCap = 2048;     // distinct penalised ids listed per CTA
 
 __device__ __forceinline__ uint32_t order32(float v) {
     uint32_t b = __float_as_uint(v);

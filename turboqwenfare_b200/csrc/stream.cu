@@ -5,18 +5,18 @@
 // Work layout. A row is split into `slices` contiguous id ranges of
 // `slice_len` ids; CTA (row, slice) streams its range from HBM exactly once
 // into registers (16-byte evict-first loads, 40 logits per thread) and then:
-//   1. applies the repetition/frequency/presence penalties of the row's
-//      window (src/sampling/mod.rs:114-148) through a per-slice count table
-//      in shared memory (u16 per id, saturating above 65,534 with an exact
-//      recount of the saturated ids);
+//   1. builds a shared-memory table of the slice's penalised logits: the
+//      row's window (src/sampling/mod.rs:114-148) is counted with atomics and
+//      each repeated id's value is penalised once, so the per-element work is
+//      a table load and a select (no division in the streaming loop);
 //   2. keeps the greedy top-4 of the raw logits (src/runtime/decode.rs:
 //      48-64) when the row is greedy or diagnostics are requested;
 //   3. for sampled rows, selects its local top-k by (value desc, id asc):
-//      a threshold theta = k-th largest per-thread maximum is a valid lower
-//      bound of the local k-th key, so filtering the registers against it
-//      yields a short candidate list (about k entries) that is ranked in
-//      shared memory; a bisection over the key space replaces the estimate
-//      if the list overflows;
+//      theta = k-th largest per-thread maximum is a lower bound of the local
+//      k-th value (k distinct elements reach it), so comparing the registers
+//      against it yields a short candidate list (about k entries) that is
+//      ranked in shared memory; a bisection over the key space replaces the
+//      estimate when the list overflows;
 //   4. writes its sorted local list to scratch and takes a ticket. The CTA
 //      that takes the last ticket merges the row's lists (every global top-k
 //      member is in its slice's local top-k), then runs softmax, top_p, min_p
@@ -35,24 +35,26 @@ namespace tqfs {
 
 namespace {
 
+constexpr uint32_t kNoPenalty = 0xFFFFFFFFu;  // table sentinel: GPU arithmetic never
+                                              // produces this NaN pattern
+
 struct Fixed {
-    unsigned long long wsort[kThreads];  // per-warp sorted thread maxima
-    unsigned long long topk[kMaxK];      // merged top-k keys (value order)
-    unsigned long long pkey[kMaxK];      // probability keys, then sorted
+    float wsort[kThreads];               // per-warp sorted thread maxima
+    unsigned long long topk[kMaxK];      // merged top-k keys, then probability keys
+    unsigned long long pkey[kMaxK];
     float e[kMaxK];
     float prob[kMaxK];                   // probabilities in draw order
     unsigned long long wtop4[kWarps][4];
     unsigned long long top4[4];
-    unsigned long long theta;
+    float theta;
+    int theta_found;
     int off[65];
-    int rc_id[kRecountCap];
-    unsigned int rc_count[kRecountCap];
-    int nrecount;
     int ncand;
     int cnt[kWarps];
     int last;
     int err;
     float total;
+    int result[2];
 };
 
 __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned long long k) {
@@ -66,13 +68,11 @@ __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned lo
         } else {
             t[1] = k;
         }
+    } else if (k > t[2]) {
+        t[3] = t[2];
+        t[2] = k;
     } else {
-        if (k > t[2]) {
-            t[3] = t[2];
-            t[2] = k;
-        } else {
-            t[3] = k;
-        }
+        t[3] = k;
     }
 }
 
@@ -93,7 +93,47 @@ __device__ __forceinline__ void warp_top4(unsigned long long t[4], unsigned long
     }
 }
 
-// Number of entries > x in a descending-sorted array.
+// Per-thread top-4 of raw logits by strict '>' (src/runtime/decode.rs:48-64):
+// elements arrive in increasing id order per thread, so among equal values
+// the earlier id keeps its place; NaN and -inf never enter.
+struct Top4 {
+    float v0 = -INFINITY, v1 = -INFINITY, v2 = -INFINITY, v3 = -INFINITY;
+    int i0 = 0, i1 = 0, i2 = 0, i3 = 0;
+    __device__ __forceinline__ void insert(float x, int id) {
+        if (!(x > v3)) return;
+        if (x > v2) {
+            v3 = v2;
+            i3 = i2;
+            if (x > v1) {
+                v2 = v1;
+                i2 = i1;
+                if (x > v0) {
+                    v1 = v0;
+                    i1 = i0;
+                    v0 = x;
+                    i0 = id;
+                } else {
+                    v1 = x;
+                    i1 = id;
+                }
+            } else {
+                v2 = x;
+                i2 = id;
+            }
+        } else {
+            v3 = x;
+            i3 = id;
+        }
+    }
+    __device__ __forceinline__ void keys(unsigned long long k[4]) const {
+        k[0] = greedy_key(v0, static_cast<uint32_t>(i0));
+        k[1] = greedy_key(v1, static_cast<uint32_t>(i1));
+        k[2] = greedy_key(v2, static_cast<uint32_t>(i2));
+        k[3] = greedy_key(v3, static_cast<uint32_t>(i3));
+    }
+};
+
+// Entries > x in a descending array.
 __device__ __forceinline__ int count_greater(const unsigned long long* arr, int n,
                                              unsigned long long x) {
     int lo = 0, hi = n;
@@ -104,15 +144,18 @@ __device__ __forceinline__ int count_greater(const unsigned long long* arr, int 
     return lo;
 }
 
-__device__ __forceinline__ int block_sum(int v, Fixed& fx, int lane, int warp) {
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) fx.cnt[warp] = v;
-    __syncthreads();
-    int s = 0;
+__device__ __forceinline__ float warp_sort_desc_f(float x, int lane) {
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += fx.cnt[w];
-    return s;
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const float o = __shfl_xor_sync(0xFFFFFFFFu, x, stride);
+            const bool desc = (lane & size) == 0;
+            const bool lower = (lane & stride) == 0;
+            x = (lower == desc) ? fmaxf(x, o) : fminf(x, o);
+        }
+    }
+    return x;
 }
 
 template <int DT>
@@ -121,11 +164,12 @@ template <>
 struct Elem<0> {
     static constexpr int kVec = 4;
     static constexpr int kSize = 4;
-    __device__ static float get(const uint4& r, int i) {
-        return __uint_as_float((&r.x)[i]);
-    }
+    __device__ static float get(const uint4& r, int i) { return __uint_as_float((&r.x)[i]); }
     __device__ static void put(uint4& r, int i, const unsigned char* p) {
         (&r.x)[i] = *reinterpret_cast<const unsigned int*>(p);
+    }
+    __device__ static float load(const unsigned char* rowp, int e) {
+        return reinterpret_cast<const float*>(rowp)[e];
     }
 };
 template <>
@@ -141,9 +185,36 @@ struct Elem<1> {
         unsigned& w = (&r.x)[i >> 1];
         w = (i & 1) ? ((w & 0xFFFFu) | (h << 16)) : ((w & 0xFFFF0000u) | h);
     }
+    __device__ static float load(const unsigned char* rowp, int e) {
+        return bf16_bits_to_f32(reinterpret_cast<const unsigned short*>(rowp)[e]);
+    }
 };
 
-template <int DT>
+// Exact k-th largest key of the slice (values staged in shared memory), by
+// bisection over the 64-bit key space. Out of line: only the overflow
+// fallback (many equal values, or k close to kMaxK) reaches it.
+__device__ __noinline__ unsigned long long bisect_kth(const float* staged, int n, int lo,
+                                                      unsigned int k, int* cnt) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long blo = 1ull, bhi = ~0ull;
+    while (blo < bhi) {
+        const unsigned long long mid = blo + ((bhi - blo) >> 1) + 1ull;
+        int c = 0;
+        for (int i = tid; i < n; i += kThreads)
+            c += make_key(order32(staged[i]), static_cast<uint32_t>(lo + i)) >= mid;
+        c = warp_sum(c);
+        __syncthreads();
+        if (lane == 0) cnt[warp] = c;
+        __syncthreads();
+        int s = 0;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += cnt[w];
+        if (s >= static_cast<int>(k)) blo = mid; else bhi = mid - 1ull;
+    }
+    return blo;
+}
+
+template <int DT, bool TOP4>
 __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
     using E = Elem<DT>;
     constexpr int VEC = E::kVec;
@@ -160,20 +231,14 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
     const uint32_t k = p.top_k;
     const bool smallk = !greedy && k != 0u && k < static_cast<uint32_t>(a.vocab) &&
                         k <= static_cast<uint32_t>(kMaxK);
-    if (!greedy && !smallk) {
-        // Rows with top_k None / >= vocab / > kMaxK take the general path.
-        if (slice == 0 && tid == 0) {
-            if (a.out_status) a.out_status[row] = TQFS_ROW_ERR_UNSUPPORTED;
-            if (a.out_token) a.out_token[row] = -1;
-        }
-        return;
-    }
+    if (!greedy && !smallk) return;  // general rows are another kernel's
     const bool want_top4 = greedy || a.out_top4 != nullptr;
     const bool pen = !greedy && !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f &&
                                   p.presence_penalty == 0.0f);
     const int lo = slice * a.slice_len;
     const int hi = min(lo + a.slice_len, a.vocab);
-    const int nchunks = (hi - lo + VEC - 1) / VEC;
+    const int n_here = hi - lo;
+    const int nchunks = (n_here + VEC - 1) / VEC;
 
     // ---- 1. stream this slice into registers ------------------------------
     const unsigned char* rowp =
@@ -195,8 +260,8 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
         }
     }
 
-    // ---- 2. penalty count table (overlaps the loads in flight) ------------
-    unsigned short* table = reinterpret_cast<unsigned short*>(dyn);
+    // ---- 2. penalised-value table (overlaps the loads in flight) ----------
+    uint32_t* table = reinterpret_cast<uint32_t*>(dyn);
     long long wstart = 0, wlen = 0;
     if (pen && a.hist_off != nullptr) {
         const long long hs = a.hist_off[row], he = a.hist_off[row + 1];
@@ -206,113 +271,120 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
         wstart = he - wlen;
     }
     const bool use_table = wlen > 0;
-    const bool saturating = wlen > 65534;
     if (tid == 0) {
         fx.err = 0;
-        fx.nrecount = 0;
-        fx.theta = 0ull;
+        fx.theta_found = 0;
         fx.ncand = 0;
     }
-    int nrc = 0;
     if (use_table) {
-        const int words = (a.slice_len + 1) >> 1;
-        unsigned int* tw = reinterpret_cast<unsigned int*>(table);
-        for (int i = tid; i < words; i += kThreads) tw[i] = 0u;
+        uint4* t4 = reinterpret_cast<uint4*>(table);
+        for (int i = tid; i < (a.slice_len >> 2); i += kThreads)
+            t4[i] = make_uint4(kNoPenalty, kNoPenalty, kNoPenalty, kNoPenalty);
         __syncthreads();
+        // Counting from the sentinel: the first increment wraps it to 0, so an
+        // entry holds count - 1. The occurrence that performs the first
+        // increment lists the id, so each repeated id is penalised once.
+        int* firsts = reinterpret_cast<int*>(dyn + static_cast<size_t>(a.slice_len) * 4);
         for (long long j = tid; j < wlen; j += kThreads) {
             const int t = a.hist[wstart + j];
             if (t >= lo && t < hi) {
-                const int off = t - lo;
-                unsigned int* word = tw + (off >> 1);
-                const int sh = (off & 1) << 4;
-                if (!saturating) {
-                    atomicAdd(word, 1u << sh);
-                } else {
-                    unsigned int old = *word;
-                    for (;;) {
-                        if (((old >> sh) & 0xFFFFu) == 0xFFFFu) break;
-                        const unsigned int prev = atomicCAS(word, old, old + (1u << sh));
-                        if (prev == old) break;
-                        old = prev;
-                    }
+                if (atomicAdd(table + (t - lo), 1u) == kNoPenalty) {
+                    const int idx = atomicAdd(&fx.ncand, 1);
+                    if (idx < kFirstsCap) firsts[idx] = t - lo;
                 }
             }
         }
         __syncthreads();
-        if (saturating) {
-            for (int i = tid; i < hi - lo; i += kThreads) {
-                if (table[i] == 0xFFFFu) {
-                    const int idx = atomicAdd(&fx.nrecount, 1);
-                    if (idx < kRecountCap) fx.rc_id[idx] = lo + i;
+        const int nfirst = fx.ncand;
+        if (nfirst <= kFirstsCap) {
+            for (int q = tid; q < nfirst; q += kThreads) {
+                const int i = firsts[q];
+                const float v = E::load(rowp, lo + i);
+                table[i] = __float_as_uint(penalise(v, table[i] + 1u, p.repeat_penalty,
+                                                    p.frequency_penalty, p.presence_penalty));
+            }
+        } else {  // more distinct ids than the list holds: scan the table
+            for (int i = tid; i < n_here; i += kThreads) {
+                const uint32_t cm1 = table[i];
+                if (cm1 != kNoPenalty) {
+                    const float v = E::load(rowp, lo + i);
+                    table[i] = __float_as_uint(penalise(v, cm1 + 1u, p.repeat_penalty,
+                                                        p.frequency_penalty, p.presence_penalty));
                 }
             }
-            __syncthreads();
-            nrc = fx.nrecount;
-            if (nrc > kRecountCap) {
-                if (tid == 0) fx.err = 1;
-                nrc = kRecountCap;
-            }
-            for (int r = 0; r < nrc; ++r) {
-                const int id = fx.rc_id[r];
-                int c = 0;
-                for (long long j = tid; j < wlen; j += kThreads) c += (a.hist[wstart + j] == id);
-                c = block_sum(c, fx, lane, warp);
-                if (tid == 0) fx.rc_count[r] = static_cast<unsigned int>(c);
-            }
-            __syncthreads();
         }
+        __syncthreads();
+        if (tid == 0) fx.ncand = 0;
     }
 
-    // ---- 3. widen, greedy top-4 of raw logits, penalise --------------------
+    // ---- 3. widen, greedy top-4 of raw logits, penalised values, max ------
     float vals[kElemsPerThread];
-    unsigned long long t4[4] = {0ull, 0ull, 0ull, 0ull};
-    unsigned long long tmax = 0ull;
+    Top4 t4;
+    float tmax = -INFINITY;
+    if (greedy) {
+        // Greedy rows: only the top-4 of the raw logits (no table, no filter).
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+            const int c = tid + j * kThreads;
+            const int e0 = lo + c * VEC;
+            if (c < nchunks) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i)
+                    if (e0 + i < hi) t4.insert(E::get(raw[j], i), e0 + i);
+            }
+        }
+    }
+    if (!greedy) {
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
         const int c = tid + j * kThreads;
         const int e0 = lo + c * VEC;
-        bool any = false;
-        unsigned int cw[VEC / 2];
-        if (use_table && c < nchunks) {
-            if constexpr (VEC == 4) {
-                const uint2 w = *reinterpret_cast<const uint2*>(table + (e0 - lo));
-                cw[0] = w.x;
-                cw[1] = w.y;
-            } else {
-                const uint4 w = *reinterpret_cast<const uint4*>(table + (e0 - lo));
-                cw[0] = w.x;
-                cw[1] = w.y;
-                cw[2] = w.z;
-                cw[3] = w.w;
-            }
+        float v[VEC];
 #pragma unroll
-            for (int q = 0; q < VEC / 2; ++q) any |= cw[q] != 0u;
+        for (int i = 0; i < VEC; ++i) v[i] = E::get(raw[j], i);
+        if (e0 + VEC > hi) {  // the slice's last, partial chunk (or none)
+#pragma unroll
+            for (int i = 0; i < VEC; ++i)
+                if (e0 + i >= hi) v[i] = __uint_as_float(0x7FC00000u);  // NaN: never selected
+        }
+        if (c < nchunks) {
+            if constexpr (TOP4) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) t4.insert(v[i], e0 + i);
+            }
+            if (use_table) {
+                uint32_t tb[VEC];
+                const uint4 w0 = *reinterpret_cast<const uint4*>(table + (e0 - lo));
+                tb[0] = w0.x;
+                tb[1] = w0.y;
+                tb[2] = w0.z;
+                tb[3] = w0.w;
+                if constexpr (VEC == 8) {
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(table + (e0 - lo) + 4);
+                    tb[4] = w1.x;
+                    tb[5] = w1.y;
+                    tb[6] = w1.z;
+                    tb[7] = w1.w;
+                }
+#pragma unroll
+                for (int i = 0; i < VEC; ++i)
+                    if (tb[i] != kNoPenalty) v[i] = __uint_as_float(tb[i]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-            const int e = e0 + i;
-            const bool valid = (c < nchunks) && (e < hi);
-            float v = E::get(raw[j], i);
-            if (want_top4 && valid) top4_insert(t4, greedy_key(v, static_cast<uint32_t>(e)));
-            if (any && valid) {
-                unsigned int cnt = (cw[i >> 1] >> ((i & 1) << 4)) & 0xFFFFu;
-                if (cnt != 0u) {
-                    if (saturating && cnt == 0xFFFFu) {
-                        for (int r = 0; r < nrc; ++r)
-                            if (fx.rc_id[r] == e) cnt = fx.rc_count[r];
-                    }
-                    v = penalise(v, cnt, p.repeat_penalty, p.frequency_penalty, p.presence_penalty);
-                }
-            }
-            vals[j * VEC + i] = v;
-            if (smallk && valid) tmax = umax64(tmax, make_key(order32(v), static_cast<uint32_t>(e)));
+            vals[j * VEC + i] = v[i];
+            tmax = fmaxf(tmax, v[i]);
         }
+    }
     }
 
     const size_t ls = static_cast<size_t>(row) * a.slices + slice;
     if (want_top4) {
+        unsigned long long t4k[4];
+        t4.keys(t4k);
         unsigned long long wt[4];
-        warp_top4(t4, wt, lane);
+        warp_top4(t4k, wt, lane);
         if (lane == 0) {
 #pragma unroll
             for (int r = 0; r < 4; ++r) fx.wtop4[warp][r] = wt[r];
@@ -320,32 +392,121 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
     }
 
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(
-        dyn + ((static_cast<size_t>(a.slice_len) * 2 + 15) & ~static_cast<size_t>(15)));
+        dyn + static_cast<size_t>(a.slice_len) * 4);
     int nloc = 0;
     if (smallk) {
-        // ---- 4. threshold from the k-th largest thread maximum ------------
-        const unsigned long long sorted = warp_sort_desc(tmax, lane);
-        fx.wsort[warp * 32 + lane] = sorted;
+        // ---- 4. theta = k-th largest thread maximum -----------------------
+        fx.wsort[warp * 32 + lane] = warp_sort_desc_f(tmax, lane);
         __syncthreads();
-        if (tmax != 0ull) {
-            int rank = 0;
+        if (k <= 32u) {
+            // One warp merges the 8 sorted lists by extraction: k rounds.
+            if (warp == 0) {
+                int ptr = 0;
+                float head = lane < kWarps ? fx.wsort[lane * 32] : __uint_as_float(0x7FC00000u);
+                float kth = -INFINITY;
+                for (uint32_t r = 0; r < k; ++r) {
+                    float m = head;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) rank += count_greater(&fx.wsort[w * 32], 32, tmax);
-            if (rank == static_cast<int>(k) - 1) fx.theta = tmax;
+                    for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+                    m = __shfl_sync(0xFFFFFFFFu, m, 0);
+                    const unsigned ball = __ballot_sync(0xFFFFFFFFu, lane < kWarps && head == m);
+                    if (ball != 0u && lane == __ffs(ball) - 1) {
+                        ++ptr;
+                        head = ptr < 32 ? fx.wsort[lane * 32 + ptr] : __uint_as_float(0x7FC00000u);
+                    }
+                    kth = m;
+                }
+                if (lane == 0) {
+                    fx.theta = kth;
+                    fx.theta_found = kth == kth;
+                }
+            }
+        } else {
+            int gt = 0, ge = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float* s = fx.wsort + w * 32;
+                int l0 = 0, h0 = 32, l1 = 0, h1 = 32;
+                while (l0 < h0) {
+                    const int m = (l0 + h0) >> 1;
+                    if (s[m] > tmax) l0 = m + 1; else h0 = m;
+                }
+                while (l1 < h1) {
+                    const int m = (l1 + h1) >> 1;
+                    if (s[m] >= tmax) l1 = m + 1; else h1 = m;
+                }
+                gt += l0;
+                ge += l1;
+            }
+            if (gt < static_cast<int>(k) && static_cast<int>(k) <= ge) {
+                fx.theta = tmax;  // every writer holds the same value
+                fx.theta_found = 1;
+            }
         }
         __syncthreads();
-        unsigned long long theta = fx.theta > 0ull ? fx.theta : 1ull;
-        for (int attempt = 0; attempt < 2; ++attempt) {
+        const float theta = fx.theta;
+        const bool take_all = !fx.theta_found || !(theta > -INFINITY);
+        // ---- 5. filter ----------------------------------------------------
+        if (!take_all) {
 #pragma unroll
             for (int j = 0; j < NCH; ++j) {
-                const int c = tid + j * kThreads;
+                float cm = vals[j * VEC];
+#pragma unroll
+                for (int i = 1; i < VEC; ++i) cm = fmaxf(cm, vals[j * VEC + i]);
+                if (cm >= theta) {
+                    const int e0 = lo + (tid + j * kThreads) * VEC;
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) {
+                        if (vals[j * VEC + i] >= theta) {
+                            const int idx = atomicAdd(&fx.ncand, 1);
+                            if (idx < kCandCap)
+                                cand[idx] = make_key(order32(vals[j * VEC + i]),
+                                                     static_cast<uint32_t>(e0 + i));
+                        }
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+                const int e0 = lo + (tid + j * kThreads) * VEC;
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) {
-                    const int e = lo + c * VEC + i;
-                    if (c < nchunks && e < hi) {
+                    if (e0 + i < hi) {
+                        const int idx = atomicAdd(&fx.ncand, 1);
+                        if (idx < kCandCap)
+                            cand[idx] = make_key(order32(vals[j * VEC + i]),
+                                                 static_cast<uint32_t>(e0 + i));
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (fx.ncand > kCandCap) {
+            // Overflow: stage the penalised values and bisect for the exact
+            // local k-th key, then keep exactly the keys >= it.
+            float* staged = reinterpret_cast<float*>(dyn);
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+                const int e0 = (tid + j * kThreads) * VEC;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i)
+                    if (e0 + i < n_here) staged[e0 + i] = vals[j * VEC + i];
+            }
+            __syncthreads();
+            const unsigned long long kth = bisect_kth(staged, n_here, lo, k, fx.cnt);
+            __syncthreads();
+            if (tid == 0) fx.ncand = 0;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+                const int e0 = lo + (tid + j * kThreads) * VEC;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    if (e0 + i < hi) {
                         const unsigned long long key =
-                            make_key(order32(vals[j * VEC + i]), static_cast<uint32_t>(e));
-                        if (key >= theta) {
+                            make_key(order32(vals[j * VEC + i]), static_cast<uint32_t>(e0 + i));
+                        if (key >= kth) {
                             const int idx = atomicAdd(&fx.ncand, 1);
                             if (idx < kCandCap) cand[idx] = key;
                         }
@@ -353,32 +514,9 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
                 }
             }
             __syncthreads();
-            if (fx.ncand <= kCandCap) break;
-            // Overflow: find the exact local k-th key by bisection.
-            unsigned long long blo = 1ull, bhi = ~0ull;
-            while (blo < bhi) {
-                const unsigned long long mid = blo + ((bhi - blo) >> 1) + 1ull;
-                int c = 0;
-#pragma unroll
-                for (int j = 0; j < NCH; ++j) {
-                    const int cc = tid + j * kThreads;
-#pragma unroll
-                    for (int i = 0; i < VEC; ++i) {
-                        const int e = lo + cc * VEC + i;
-                        if (cc < nchunks && e < hi)
-                            c += make_key(order32(vals[j * VEC + i]), static_cast<uint32_t>(e)) >= mid;
-                    }
-                }
-                c = block_sum(c, fx, lane, warp);
-                if (c >= static_cast<int>(k)) blo = mid; else bhi = mid - 1ull;
-            }
-            theta = blo;
-            __syncthreads();
-            if (tid == 0) fx.ncand = 0;
-            __syncthreads();
         }
         nloc = min(fx.ncand, kCandCap);
-        // ---- 5. rank the candidates, keep the local top-k -----------------
+        // ---- 6. rank the candidates, keep the local top-k -----------------
         unsigned long long* out = a.cand + ls * kMaxK;
         for (int idx = tid; idx < nloc; idx += kThreads) {
             const unsigned long long key = cand[idx];
@@ -392,7 +530,6 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
     if (tid == 0) {
         if (smallk) a.cand_n[ls] = fx.err ? -1 : nloc;
         if (want_top4) {
-            // Merge the 8 warp lists into the slice's top-4.
             unsigned long long m[4] = {0ull, 0ull, 0ull, 0ull};
             for (int w = 0; w < kWarps; ++w)
                 for (int r = 0; r < 4; ++r) top4_insert(m, fx.wtop4[w][r]);
@@ -404,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
         for (int e = lo + tid; e < hi; e += kThreads) pr[e] = 0.0f;
     }
 
-    // ---- 6. ticket: the last CTA of the row finalises ----------------------
+    // ---- 7. ticket: the last CTA of the row finalises ----------------------
     __threadfence();
     __syncthreads();
     if (tid == 0) {
@@ -416,12 +553,15 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
     __threadfence();
 
     int token = 0;
+    unsigned long long* g = reinterpret_cast<unsigned long long*>(dyn);
     if (want_top4) {
+        const int n4 = a.slices * 4;
+        for (int i = tid; i < n4; i += kThreads)
+            g[i] = __ldcg(a.top4 + static_cast<size_t>(row) * a.slices * 4 + i);
+        __syncthreads();
         if (tid == 0) {
             unsigned long long m[4] = {0ull, 0ull, 0ull, 0ull};
-            for (int s = 0; s < a.slices; ++s)
-                for (int r = 0; r < 4; ++r)
-                    top4_insert(m, __ldcg(a.top4 + (static_cast<size_t>(row) * a.slices + s) * 4 + r));
+            for (int i = 0; i < n4; ++i) top4_insert(m, g[i]);
             for (int r = 0; r < 4; ++r) fx.top4[r] = m[r];
             if (a.out_top4 != nullptr) {
                 for (int r = 0; r < 4; ++r) {
@@ -438,17 +578,19 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
 
     int status = TQFS_ROW_OK;
     if (smallk) {
-        // ---- 7. merge the slices' sorted lists into the row's top-k -------
-        unsigned long long* g = reinterpret_cast<unsigned long long*>(dyn);
+        // ---- 8. merge the slices' sorted lists into the row's top-k -------
+        if (tid < a.slices)
+            fx.off[tid + 1] = __ldcg(a.cand_n + static_cast<size_t>(row) * a.slices + tid);
+        __syncthreads();
         if (tid == 0) {
             int acc = 0;
+            fx.off[0] = 0;
             for (int s = 0; s < a.slices; ++s) {
-                fx.off[s] = acc;
-                const int n = __ldcg(a.cand_n + static_cast<size_t>(row) * a.slices + s);
+                const int n = fx.off[s + 1];
                 if (n < 0) fx.err = 1;
                 acc += n > 0 ? n : 0;
+                fx.off[s + 1] = acc;
             }
-            fx.off[a.slices] = acc;
         }
         __syncthreads();
         const int total_n = fx.off[a.slices];
@@ -471,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
         __syncthreads();
         const int kk = min(static_cast<int>(k), total_n);
 
-        // ---- 8. softmax over the survivors (src/sampling/mod.rs:166-190) --
+        // ---- 9. softmax over the survivors (src/sampling/mod.rs:166-190) --
         const float first = kk > 0 ? key_value(fx.topk[0]) : 0.0f;
         const float mx = (kk > 0 && first == first) ? first : -INFINITY;
         if (tid < kk) {
@@ -497,11 +639,11 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
         if (tid < kk) {
             int r = 0;
             for (int q = 0; q < kk; ++q) r += fx.pkey[q] > pk;
-            fx.topk[r] = pk;  // reuse: now probability keys in draw order
+            fx.topk[r] = pk;  // probability keys in draw order
             fx.prob[r] = pv;
         }
         __syncthreads();
-        // ---- 9. top_p, min_p, draw (src/sampling/mod.rs:195-248) ----------
+        // ---- 10. top_p, min_p, draw (src/sampling/mod.rs:195-248) ---------
         if (tid == 0) {
             int keep = kk;
             if (!(p.top_p >= 1.0f)) {
@@ -521,8 +663,9 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
                 while (n < keep && fx.prob[n] >= floor) ++n;
                 keep = n < 1 ? 1 : n;
             }
-            int pick = 0;
+            int tok = 0;
             if (keep > 0) {
+                int pick = 0;
                 float total2 = -0.0f;
                 for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, fx.prob[i]);
                 if (isfinite(total2) && total2 > 0.0f) {
@@ -541,22 +684,22 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
                     pick = keep - 1;
                     for (int i = 0; i < keep; ++i) {
                         cum = __fadd_rn(cum, fx.prob[i]);
-                        if (cum >= target) { pick = i; break; }
+                        if (cum >= target) {
+                            pick = i;
+                            break;
+                        }
                     }
                 }
-                token = static_cast<int>(key_token(fx.topk[pick]));
-            } else {
-                token = 0;
+                tok = static_cast<int>(key_token(fx.topk[pick]));
             }
-            fx.off[0] = token;
-            fx.off[1] = keep;
+            fx.result[0] = tok;
+            fx.result[1] = keep;
         }
         __syncthreads();
-        token = fx.off[0];
-        const int keep = fx.off[1];
-        if (a.out_probs != nullptr && tid < keep) {
+        token = fx.result[0];
+        const int keep = fx.result[1];
+        if (a.out_probs != nullptr && tid < keep)
             a.out_probs[static_cast<size_t>(row) * a.ld + key_token(fx.topk[tid])] = fx.prob[tid];
-        }
         if (fx.err) status = TQFS_ROW_ERR_WINDOW;
     }
     if (tid == 0) {
@@ -584,8 +727,7 @@ Plan plan_stream(int vocab) {
     if (pl.slices < 1) pl.slices = 1;
     const int per = (vocab + pl.slices - 1) / pl.slices;
     pl.slice_len = (per + 7) & ~7;
-    const size_t table = (static_cast<size_t>(pl.slice_len) * 2 + 15) & ~static_cast<size_t>(15);
-    const size_t work = table + static_cast<size_t>(kCandCap) * 8;
+    const size_t work = static_cast<size_t>(pl.slice_len) * 4 + static_cast<size_t>(kCandCap) * 8;
     const size_t gather = static_cast<size_t>(pl.slices) * kMaxK * 8;
     pl.smem = work > gather ? work : gather;
     return pl;
@@ -594,15 +736,14 @@ Plan plan_stream(int vocab) {
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s) {
     const long long grid = static_cast<long long>(a.rows) * plan.slices;
     if (grid <= 0) return cudaSuccess;
-    if (a.dtype == TQFS_DTYPE_F32) {
-        cudaFuncSetAttribute(stream_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(plan.smem));
-        stream_kernel<0><<<static_cast<unsigned>(grid), kThreads, plan.smem, s>>>(a);
-    } else {
-        cudaFuncSetAttribute(stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(plan.smem));
-        stream_kernel<1><<<static_cast<unsigned>(grid), kThreads, plan.smem, s>>>(a);
-    }
+    // Diagnostics (top-4 of sampled rows) use their own instantiation so the
+    // common path carries no top-4 state in its registers.
+    const bool top4 = a.out_top4 != nullptr && !a.top4_only;
+    void (*kern)(SampleArgs);
+    if (a.dtype == TQFS_DTYPE_F32) kern = top4 ? stream_kernel<0, true> : stream_kernel<0, false>;
+    else kern = top4 ? stream_kernel<1, true> : stream_kernel<1, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem));
+    kern<<<static_cast<unsigned>(grid), kThreads, plan.smem, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -610,70 +751,6 @@ cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,
                               tqfs_candidate* out_top4, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     fill_empty_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token, out_status, out_top4);
-    return cudaGetLastError();
-}
-
-}  // namespace tqfs
-
-// ---- penalties inspection kernels --------------------------------------------
-namespace tqfs {
-namespace {
-
-__global__ void widen_kernel(const void* logits, int dtype, int vocab, long long ld, float* out) {
-    const int row = blockIdx.y;
-    const size_t base = static_cast<size_t>(row) * ld;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
-        float v;
-        if (dtype == TQFS_DTYPE_F32) v = static_cast<const float*>(logits)[base + i];
-        else v = bf16_bits_to_f32(static_cast<const unsigned short*>(logits)[base + i]);
-        out[base + i] = v;
-    }
-}
-
-// One CTA per row: every window token that is the last occurrence of its id
-// counts the id's occurrences and writes the penalised value.
-__global__ void penalties_kernel(const void* logits, int dtype, int vocab, long long ld,
-                                 const int32_t* hist, const int64_t* hist_off,
-                                 const tqfs_params* params, float* out) {
-    const int row = blockIdx.x;
-    const tqfs_params p = params[row];
-    if (p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f && p.presence_penalty == 0.0f)
-        return;
-    if (hist_off == nullptr) return;
-    const long long hs = hist_off[row], he = hist_off[row + 1];
-    const unsigned long long len = he > hs ? static_cast<unsigned long long>(he - hs) : 0ull;
-    const long long w = static_cast<long long>(p.repeat_last_n < len ? p.repeat_last_n : len);
-    const long long ws = he - w;
-    const size_t base = static_cast<size_t>(row) * ld;
-    for (long long j = threadIdx.x; j < w; j += blockDim.x) {
-        const int t = hist[ws + j];
-        if (t < 0 || t >= vocab) continue;
-        bool last = true;
-        unsigned int count = 1;
-        for (long long q = 0; q < w; ++q) {
-            if (q == j) continue;
-            if (hist[ws + q] == t) {
-                ++count;
-                if (q > j) last = false;
-            }
-        }
-        if (!last) continue;
-        float v;
-        if (dtype == TQFS_DTYPE_F32) v = static_cast<const float*>(logits)[base + t];
-        else v = bf16_bits_to_f32(static_cast<const unsigned short*>(logits)[base + t]);
-        out[base + t] = penalise(v, count, p.repeat_penalty, p.frequency_penalty, p.presence_penalty);
-    }
-}
-
-}  // namespace
-
-cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,
-                             const int32_t* hist, const int64_t* hist_off,
-                             const tqfs_params* params, float* out, cudaStream_t s) {
-    if (rows <= 0 || vocab <= 0) return cudaSuccess;
-    dim3 g((vocab + 1023) / 1024 < 64 ? (vocab + 1023) / 1024 : 64, rows);
-    widen_kernel<<<g, 1024, 0, s>>>(logits, dtype, vocab, ld, out);
-    penalties_kernel<<<rows, 256, 0, s>>>(logits, dtype, vocab, ld, hist, hist_off, params, out);
     return cudaGetLastError();
 }
 
