@@ -184,6 +184,32 @@ int tqfs_apply_penalties(tqfs_handle* handle, const void* logits_dev, int dtype,
                          const int64_t* hist_off_dev, const tqfs_params* params_dev,
                          float* out_dev, void* stream);
 
+/*
+ * tqfs_sample without any GPU allocation. No counterpart in the reference
+ * (its sampler is host code); it exists for callers that cannot call
+ * cudaMalloc: hosts whose GPU memory is already reserved by their own pool,
+ * where an allocation of ours would fail or fragment it, and decode loops
+ * where cudaMalloc/cudaFree would synchronise the device. Same arguments as
+ * tqfs_sample without the handle and the optional diagnostics; out_token_dev
+ * and out_status_dev are required.
+ *   - Scratch is a fixed 8.5 MiB __device__ array present on every GPU that
+ *     loads the library until the process exits: rows * ceil(vocab/10,240)
+ *     must be <= 4,096 and rows <= 4,096 (256 rows at vocab 151,936), else
+ *     TQFS_ERR_UNSUPPORTED and nothing is launched.
+ *   - Runs greedy rows and rows with top_k in [1, 256] below vocab; other rows
+ *     get status TQFS_ROW_ERR_UNSUPPORTED and token -1.
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the array and leave its contents behind; the parts that
+ *     must start at zero are cleared on `stream` at the start of each call.
+ *     Calls that overlap on the GPU race on it and must not be issued.
+ */
+int tqfs_sample_static(const void* logits_dev, int dtype, int rows, int vocab, int64_t ld,
+                       const int32_t* hist_dev, const int64_t* hist_off_dev,
+                       const tqfs_params* params_dev, const float* uniforms_dev,
+                       uint64_t* rng_state_dev, int32_t* out_token_dev,
+                       int32_t* out_status_dev, void* stream);
+
 /* ---- drop-in Sampler (host pointers; synchronising) ---------------------- */
 /*
  * `Sampler::new(&SamplingParams)` (src/sampling/mod.rs:45-53): greedy iff
