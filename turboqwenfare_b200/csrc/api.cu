@@ -53,6 +53,8 @@ struct tqfs_handle {
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer tickets;      // per-row tickets, kept zero between launches
     size_t ticket_rows = 0;
+    DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
+    size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
     DeviceBuffer h_logits, h_hist, h_off, h_params, h_unif, h_rng, h_tok;
     cudaStream_t own_stream = nullptr;
@@ -194,6 +196,41 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
         cudaMemsetAsync(h->tickets.ptr, 0, h->tickets.bytes, s);
         return cuda_fail(h, e, "stream kernel launch");
     }
+    if (a.top4_only) return TQFS_OK;
+    // Rows the stream kernel does not own run the general kernel.
+    const int ctas = a.rows < 64 ? a.rows : 64;
+    size_t stride = 0, key_stride = 0;
+    const size_t bytes = tqfs::general_scratch_bytes(a.vocab, ctas, &stride, &key_stride);
+    const bool relayout = h->general_layout[0] != stride || h->general_layout[1] != key_stride ||
+                          h->general_layout[2] < static_cast<size_t>(ctas);
+    if (relayout) {
+        const size_t keep_ctas = h->general_layout[2] > static_cast<size_t>(ctas)
+                                     ? h->general_layout[2] : static_cast<size_t>(ctas);
+        const size_t need = tqfs::general_scratch_bytes(a.vocab, static_cast<int>(keep_ctas),
+                                                        &stride, &key_stride);
+        e = h->general.reserve(need);
+        if (e != cudaSuccess) return cuda_fail(h, e, "general scratch allocation");
+        e = cudaMemsetAsync(h->general.ptr, 0, h->general.bytes, s);
+        if (e != cudaSuccess) return cuda_fail(h, e, "general scratch reset");
+        h->general_layout[0] = stride;
+        h->general_layout[1] = key_stride;
+        h->general_layout[2] = keep_ctas;
+    }
+    (void)bytes;
+    const size_t cap = h->general_layout[2];
+    unsigned char* gb = static_cast<unsigned char*>(h->general.ptr);
+    tqfs::GeneralScratch g;
+    g.stride = stride;
+    g.key_stride = key_stride;
+    g.work = reinterpret_cast<float*>(gb);
+    g.counts = reinterpret_cast<unsigned int*>(gb + cap * stride * 4);
+    g.e = reinterpret_cast<float*>(gb + cap * stride * 8);
+    g.keys = reinterpret_cast<unsigned long long*>(gb + cap * stride * 12);
+    {
+        TimingScope ts(h, s, 1);
+        e = tqfs::launch_general(a, g, ctas, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "general kernel launch");
     return TQFS_OK;
 }
 
@@ -259,6 +296,7 @@ int tqfs_destroy(tqfs_handle* h) {
     for (cudaEvent_t e : h->free_events) cudaEventDestroy(e);
     h->scratch.release();
     h->tickets.release();
+    h->general.release();
     h->h_logits.release();
     h->h_hist.release();
     h->h_off.release();

@@ -37,6 +37,16 @@ struct SampleArgs {
     int top4_only;   // tqfs_top_logit_candidates: every row is greedy
 };
 
+// Per-CTA working arrays of the general kernel (library scratch).
+struct GeneralScratch {
+    float* work;               // penalised logits, then candidate tokens
+    unsigned int* counts;      // window counts, kept zero between rows
+    float* e;                  // exp((v - max) / T), candidate order
+    unsigned long long* keys;  // order keys for the bitonic sorts
+    size_t stride;             // elements per CTA in work / counts / e
+    size_t key_stride;         // keys per CTA (a power of two >= vocab)
+};
+
 struct Plan {
     int slices;
     int slice_len;
@@ -45,6 +55,8 @@ struct Plan {
 
 Plan plan_stream(int vocab);
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s);
+size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
+cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s);
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,
                              const int32_t* hist, const int64_t* hist_off,
                              const tqfs_params* params, float* out, cudaStream_t s);
