@@ -51,7 +51,8 @@ enum tqfs_row_status {
     TQFS_ROW_OK = 0,
     TQFS_ROW_ERR_WINDOW = 1,      /* penalty window beyond the supported size */
     TQFS_ROW_ERR_UNSUPPORTED = 2, /* row needs a path this build lacks        */
-    TQFS_ROW_ERR_EMPTY = 4        /* vocab == 0: token 0, as the reference    */
+    TQFS_ROW_ERR_EMPTY = 4,       /* vocab == 0: token 0, as the reference    */
+    TQFS_ROW_ERR_TIMEOUT = 8      /* a time-bounded wait on a copy gave up    */
 };
 
 /* ---- sampling parameters ---------------------------------------------- */
@@ -192,17 +193,19 @@ int tqfs_apply_penalties(tqfs_handle* handle, const void* logits_dev, int dtype,
  * where cudaMalloc/cudaFree would synchronise the device. Same arguments as
  * tqfs_sample without the handle and the optional diagnostics; out_token_dev
  * and out_status_dev are required.
- *   - Scratch is a fixed 8.5 MiB __device__ array present on every GPU that
- *     loads the library until the process exits: rows * ceil(vocab/10,240)
- *     must be <= 4,096 and rows <= 4,096 (256 rows at vocab 151,936), else
- *     TQFS_ERR_UNSUPPORTED and nothing is launched.
- *   - Runs greedy rows and rows with top_k in [1, 256] below vocab; other rows
- *     get status TQFS_ROW_ERR_UNSUPPORTED and token -1.
+ *   - Scratch is a fixed 48 MiB __device__ array present on every GPU that
+ *     loads the library until the process exits. At vocab 151,936 a row
+ *     needs 34 to 48 KiB (the split of rows into work units depends on the
+ *     batch), so up to about 1,300 rows fit; a call that needs more returns
+ *     TQFS_ERR_UNSUPPORTED and launches nothing.
+ *   - Runs greedy rows and rows with top_k in [1, 128] below vocab whose
+ *     penalty window is at most 8,192 tokens; other rows get status
+ *     TQFS_ROW_ERR_UNSUPPORTED and token -1.
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
- *   - All calls share the array and leave its contents behind; the parts that
- *     must start at zero are cleared on `stream` at the start of each call.
- *     Calls that overlap on the GPU race on it and must not be issued.
+ *   - All calls share the array and leave its contents behind; no part of
+ *     it needs clearing, as each call writes what it later reads. Calls that
+ *     overlap on the GPU race on it and must not be issued.
  */
 int tqfs_sample_static(const void* logits_dev, int dtype, int rows, int vocab, int64_t ld,
                        const int32_t* hist_dev, const int64_t* hist_off_dev,

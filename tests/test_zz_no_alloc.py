@@ -67,7 +67,7 @@ def test_static_scratch_matches_the_allocating_entry_point_on_consecutive_calls(
 def test_rows_outside_the_stream_kernel_report_unsupported(cuda_device):
     b = W.config("c1", rows=6, seed=33, vocab=20_000)
     b.params["top_k"][1] = 0        # full-vocabulary row: not this kernel's
-    b.params["top_k"][4] = 1000     # top_k above 256: not this kernel's
+    b.params["top_k"][4] = 1000     # top_k above 128: not this kernel's
     import torch
     lg, hist, off, par, uni = _device_batch(b)
     tok = torch.empty(6, dtype=torch.int32, device="cuda")
@@ -87,8 +87,8 @@ def test_batches_beyond_the_fixed_scratch_are_rejected_without_a_launch(cuda_dev
     import torch
     x = torch.zeros(1, dtype=torch.float32, device="cuda")
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
-    # 300 rows at vocab 151,936 need 300 * 15 work items > 4,096.
-    rc = N.lib().tqfs_sample_static(x.data_ptr(), N.DTYPE_F32, 300, 151_936, 151_936, None, None,
+    # 2,000 rows at vocab 151,936 need about 72 MiB of scratch > 48 MiB.
+    rc = N.lib().tqfs_sample_static(x.data_ptr(), N.DTYPE_F32, 2000, 151_936, 151_936, None, None,
                                     x.data_ptr(), x.data_ptr(), None, out.data_ptr(), out.data_ptr(),
                                     torch.cuda.current_stream().cuda_stream)
     assert rc == N.ERR_UNSUPPORTED

@@ -29,6 +29,7 @@ ROW_OK = 0
 ROW_ERR_WINDOW = 1
 ROW_ERR_UNSUPPORTED = 2
 ROW_ERR_EMPTY = 4
+ROW_ERR_TIMEOUT = 8
 
 PARAM_HAS_MIN_P = 1
 

@@ -51,9 +51,9 @@ struct tqfs_handle {
     int device = 0;
     std::string error;
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
-    DeviceBuffer tickets;      // per-row tickets, kept zero between launches
-    size_t ticket_rows = 0;
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
+    DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
+    uint32_t epoch = 0;        // number of the last call
     size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
     DeviceBuffer h_logits, h_hist, h_off, h_params, h_unif, h_rng, h_tok;
@@ -147,27 +147,22 @@ int ensure_current(tqfs_handle* h) {
     return TQFS_OK;
 }
 
-// Scratch for the stream kernel; tickets are zeroed when (re)allocated and
-// the kernel leaves them zero.
-int ensure_scratch(tqfs_handle* h, int rows, int slices, tqfs::SampleArgs& a) {
-    const size_t ls = static_cast<size_t>(rows) * slices;
-    const size_t cand = ls * tqfs::kMaxK * 8;
-    const size_t cn = (ls * 4 + 255) & ~static_cast<size_t>(255);
-    const size_t t4 = ls * 4 * 8;
-    cudaError_t e = h->scratch.reserve(cand + cn + t4);
+// Scratch of the stream path (candidate lists, chunk bounds, greedy lists,
+// window buckets), grown on demand and never cleared: every field a kernel
+// reads is written earlier in the same call.
+int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::SampleArgs& a) {
+    const size_t bytes = tqfs::stream_scratch(rows, plan, nullptr, nullptr);
+    cudaError_t e = h->scratch.reserve(bytes);
     if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
-    if (static_cast<size_t>(rows) > h->ticket_rows) {
-        e = h->tickets.reserve(static_cast<size_t>(rows) * 4);
-        if (e != cudaSuccess) return cuda_fail(h, e, "ticket allocation");
-        e = cudaMemset(h->tickets.ptr, 0, h->tickets.bytes);
-        if (e != cudaSuccess) return cuda_fail(h, e, "ticket reset");
-        h->ticket_rows = h->tickets.bytes / 4;
+    tqfs::stream_scratch(rows, plan, h->scratch.ptr, &a);
+    if (h->err_word.ptr == nullptr) {  // zero once; calls are told apart by epoch
+        e = h->err_word.reserve(16);
+        if (e == cudaSuccess) e = cudaMemset(h->err_word.ptr, 0, 16);
+        if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     }
-    unsigned char* base = static_cast<unsigned char*>(h->scratch.ptr);
-    a.cand = reinterpret_cast<unsigned long long*>(base);
-    a.cand_n = reinterpret_cast<int*>(base + cand);
-    a.top4 = reinterpret_cast<unsigned long long*>(base + cand + cn);
-    a.ticket = static_cast<unsigned int*>(h->tickets.ptr);
+    if (++h->epoch == 0u) h->epoch = 1u;
+    a.err_word = static_cast<uint32_t*>(h->err_word.ptr);
+    a.epoch = h->epoch;
     return TQFS_OK;
 }
 
@@ -179,12 +174,10 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
         cudaError_t e = tqfs::launch_fill_empty(a.rows, a.out_token, a.out_status, a.out_top4, s);
         return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "launch");
     }
-    const tqfs::Plan plan = tqfs::plan_stream(a.vocab);
-    if (plan.slices > 64) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
-    int st = ensure_scratch(h, a.rows, plan.slices, a);
+    const tqfs::Plan plan = tqfs::plan_stream(a.rows, a.vocab, a.dtype);
+    if (plan.chunks == 0) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
+    int st = ensure_scratch(h, a.rows, plan, a);
     if (st != TQFS_OK) return st;
-    a.slices = plan.slices;
-    a.slice_len = plan.slice_len;
     const size_t esz = a.dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
     cudaError_t e;
@@ -192,10 +185,7 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
         TimingScope ts(h, s, 0);
         e = tqfs::launch_stream(a, plan, s);
     }
-    if (e != cudaSuccess) {
-        cudaMemsetAsync(h->tickets.ptr, 0, h->tickets.bytes, s);
-        return cuda_fail(h, e, "stream kernel launch");
-    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
     if (a.top4_only) return TQFS_OK;
     // Rows the stream kernel does not own run the general kernel.
     const int ctas = a.rows < 64 ? a.rows : 64;
@@ -295,8 +285,8 @@ int tqfs_destroy(tqfs_handle* h) {
     drain_timing(h);
     for (cudaEvent_t e : h->free_events) cudaEventDestroy(e);
     h->scratch.release();
-    h->tickets.release();
     h->general.release();
+    h->err_word.release();
     h->h_logits.release();
     h->h_hist.release();
     h->h_off.release();

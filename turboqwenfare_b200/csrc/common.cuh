@@ -21,13 +21,40 @@
 
 namespace tqfs {
 
-constexpr int kThreads = 256;        // threads per CTA of the stream kernel
-constexpr int kWarps = kThreads / 32;
-constexpr int kElemsPerThread = 40;  // logits held in registers per thread
-constexpr int kMaxSliceLen = kThreads * kElemsPerThread;  // 10,240 ids
-constexpr int kMaxK = 256;           // top_k handled by the stream kernel
-constexpr int kCandCap = 1024;       // per-CTA candidate list capacity
-constexpr int kFirstsCap = 2048;     // distinct penalised ids listed per CTA
+constexpr int kStreamMaxK = 128;     // largest top_k the stream path owns
+constexpr int kChunkCap = 256;       // candidate keys kept per (row, chunk)
+constexpr int kWinCap = 8192;        // penalty-window tokens the stream path buckets
+constexpr int kMaxChunks = 512;      // chunks per row (8 KiB of logits each)
+
+// Which kernel owns a row.
+enum : int { kModeGreedy = 0, kModeStream = 1, kModeGeneral = 2 };
+
+// Routing shared by every kernel of a call, computed from the same device
+// data so the kernels agree: greedy rows (temperature == 0, mod.rs:45-51)
+// and sampled rows with 0 < top_k <= kStreamMaxK, top_k < vocab and a
+// penalty window of at most kWinCap tokens go to the stream path; all other
+// sampled rows to the general kernel. The window is the last
+// min(repeat_last_n, len) history tokens (mod.rs:120-126) and is empty when
+// every penalty is neutral (mod.rs:115-119).
+__device__ __forceinline__ int row_mode(const tqfs_params& p, long long hs, long long he,
+                                        bool has_hist, int vocab, bool top4_only,
+                                        long long* wstart, long long* wlen) {
+    *wstart = 0;
+    *wlen = 0;
+    if (top4_only || p.temperature == 0.0f) return kModeGreedy;
+    const uint32_t k = p.top_k;
+    const bool small_k = k != 0u && k < static_cast<uint32_t>(vocab) &&
+                         k <= static_cast<uint32_t>(kStreamMaxK);
+    if (has_hist &&
+        !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f && p.presence_penalty == 0.0f)) {
+        const unsigned long long len = he > hs ? static_cast<unsigned long long>(he - hs) : 0ull;
+        const unsigned long long w = p.repeat_last_n < len ? p.repeat_last_n : len;
+        *wlen = static_cast<long long>(w);
+        *wstart = he - static_cast<long long>(w);
+        if (w > static_cast<unsigned long long>(kWinCap)) return kModeGeneral;
+    }
+    return small_k ? kModeStream : kModeGeneral;
+}
 
 __device__ __forceinline__ uint32_t order32(float v) {
     uint32_t b = __float_as_uint(v);
@@ -102,6 +129,12 @@ __device__ __forceinline__ float xoshiro_next_f32(uint64_t s[4]) {
                      16777216.0f);
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ uint64_t umax64(uint64_t a, uint64_t b) { return a > b ? a : b; }
 __device__ __forceinline__ uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
@@ -135,6 +168,68 @@ __device__ __forceinline__ int warp_sum(int x) {
 // Streaming 16-byte load: read once, evict first.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+
+// Smallest float f such that, for every non-NaN v, v >= f exactly when
+// order32(v) >= t (t >= 1). Order values with no float of their own (the
+// NaN encodings and the slot of -0.0) map to the next float above them.
+__device__ __forceinline__ float ord_threshold(uint32_t t) {
+    if (t <= 0x007FFFFFu) return -INFINITY;                         // at or below -inf
+    if (t > 0xFF800000u) return __uint_as_float(0x7FC00000u);      // above +inf: nothing
+    return from_order32(t);                                         // 0x7FFFFFFF -> -0.0
+}
+
+// ---- mbarrier + bulk copy (non-tensor, no multicast) ---------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Orders this thread's (and, after a warp barrier, its warp's) earlier
+// generic-proxy accesses of shared memory before later async-proxy writes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+// Global -> this CTA's shared memory; completion is counted on `bar` in
+// bytes. dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+// Wait on an mbarrier phase for at most ~budget_ns: false when it gave up
+// (the caller reports an error instead of spinning forever).
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity,
+                                                  unsigned long long budget_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > budget_ns) return false;
+    }
+    return true;
 }
 
 }  // namespace tqfs

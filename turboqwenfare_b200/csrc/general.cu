@@ -1,5 +1,6 @@
 // General kernel: the sampled rows the stream kernel does not own (top_k
-// None/0, top_k >= vocab, or top_k > kMaxK). These rows run the reference's
+// None/0, top_k >= vocab, top_k > kStreamMaxK, or a penalty window longer
+// than kWinCap). These rows run the reference's
 // full filter chain over up to the whole vocabulary, and its result depends
 // on the f32 rounding of three sequential sums the reference performs
 // (src/sampling/mod.rs:180, 199-207, 234-245): over ~150k terms those sums
@@ -27,10 +28,14 @@ namespace {
 
 constexpr int kGenThreads = 512;
 
-__device__ __forceinline__ bool is_general(const tqfs_params& p, int vocab) {
-    if (p.temperature == 0.0f) return false;
-    const uint32_t k = p.top_k;
-    return !(k != 0u && k < static_cast<uint32_t>(vocab) && k <= static_cast<uint32_t>(kMaxK));
+// Rows the stream path does not own (row_mode in common.cuh).
+__device__ __forceinline__ bool is_general(const SampleArgs& a, int row, const tqfs_params& p) {
+    long long hs = 0, he = 0, ws, wl;
+    if (a.hist_off != nullptr) {
+        hs = a.hist_off[row];
+        he = a.hist_off[row + 1];
+    }
+    return row_mode(p, hs, he, a.hist_off != nullptr, a.vocab, false, &ws, &wl) == kModeGeneral;
 }
 
 __device__ __forceinline__ float block_max(float v, float* red) {
@@ -90,7 +95,7 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
 
     for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
         const tqfs_params p = a.params[row];
-        if (!is_general(p, V)) continue;
+        if (!is_general(a, row, p)) continue;
         const size_t base = static_cast<size_t>(row) * a.ld;
         // ---- penalised candidates in token order (mod.rs:90-99, 114-148) --
         for (int i = tid; i < V; i += kGenThreads) W[i] = logit_at<DT>(a.logits, base, i);

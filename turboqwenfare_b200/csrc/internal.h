@@ -26,15 +26,21 @@ struct SampleArgs {
     tqfs_candidate* out_top4;
     float* out_probs;
     int32_t* out_status;
-    // library scratch
-    unsigned long long* cand;  // rows x slices x kMaxK candidate keys
-    int* cand_n;               // rows x slices
-    unsigned long long* top4;  // rows x slices x 4 greedy keys
-    unsigned int* ticket;      // rows, zero between launches
-    int slices;
-    int slice_len;
-    int vec_ok;      // rows start on 16-byte boundaries
-    int top4_only;   // tqfs_top_logit_candidates: every row is greedy
+    // library scratch (layout from stream_scratch)
+    unsigned long long* cand;  // rows x units x kUnitCap candidate keys
+    int* cand_n;               // rows x units: keys written per unit
+    uint32_t* theta;           // rows x units: order value the unit's top-k reaches
+    unsigned long long* top4;  // rows x units x 4 greedy keys
+    uint32_t* win_off;         // rows x chunks x 2: [start, end) of a chunk's window entries
+    uint32_t* win_ent;         // rows x kWinCap: distinct window ids per chunk, (id << 16) | count
+    int chunks;                // chunks per row
+    int chunk_len;             // ids per chunk
+    int unit_len;              // chunks per unit (a warp's run of one row)
+    int units;                 // units per row
+    uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
+    uint32_t epoch;            // this call's number (never 0)
+    int vec_ok;                // rows start on 16-byte boundaries
+    int top4_only;             // tqfs_top_logit_candidates: every row is greedy
 };
 
 // Per-CTA working arrays of the general kernel (library scratch).
@@ -48,12 +54,19 @@ struct GeneralScratch {
 };
 
 struct Plan {
-    int slices;
-    int slice_len;
-    size_t smem;
+    int chunks;
+    int chunk_len;
+    int unit_len;
+    int units;
+    size_t smem;  // dynamic shared memory of the stream kernel
 };
 
-Plan plan_stream(int vocab);
+// chunks == 0 when the vocabulary needs more than kMaxChunks chunks. The
+// unit length depends on rows (work balance over the device's warps).
+Plan plan_stream(int rows, int vocab, int dtype);
+// Bytes of stream-path scratch for `rows`; with a non-null base, also points
+// a's scratch fields into [base, base + bytes).
+size_t stream_scratch(int rows, const Plan& plan, void* base, SampleArgs* a);
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
 cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s);

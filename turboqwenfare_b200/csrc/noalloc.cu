@@ -10,13 +10,15 @@
 // the scratch is a file-scope __device__ array that exists on every GPU that
 // loads the library, for as long as the process runs.
 //
-// Limits and sharing. The array holds kStaticPairs (row, slice) work items
-// and kStaticRows row tickets: rows * ceil(vocab / 10,240) <= 4,096 and
-// rows <= 4,096 (256 rows at vocab 151,936). Every call on a device uses the
-// same array and leaves its contents behind; the tickets, which must start at
-// zero, are cleared on the caller's stream at the start of each call. Calls
-// that overlap on the GPU (different streams, or host threads without
-// ordering) race on the array and must not be issued.
+// Limits and sharing. The array is kStaticBytes (48 MiB) and holds the
+// stream path's per-row scratch: 34 to 48 KiB per row at vocab 151,936 (the
+// split of rows into work units depends on the batch), so up to about 1,300
+// rows of that width; a call that needs more returns TQFS_ERR_UNSUPPORTED.
+// Every call on a device uses the same array and leaves its contents behind;
+// nothing in it has to start at zero, because every field a kernel reads is
+// written earlier in the same call. Calls that overlap on the GPU (different
+// streams, or host threads without ordering) race on the array and must not
+// be issued.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -27,19 +29,16 @@
 namespace tqfs {
 namespace {
 
-constexpr int kStaticPairs = 4096;
-constexpr int kStaticRows = 4096;
-constexpr size_t kCandBytes = static_cast<size_t>(kStaticPairs) * kMaxK * 8;  // 8 MiB
-constexpr size_t kCountBytes = static_cast<size_t>(kStaticPairs) * 4;        // 16 KiB
-constexpr size_t kTop4Bytes = static_cast<size_t>(kStaticPairs) * 4 * 8;     // 128 KiB
-constexpr size_t kTicketBytes = static_cast<size_t>(kStaticRows) * 4;        // 16 KiB
-constexpr size_t kStaticBytes = kCandBytes + kCountBytes + kTop4Bytes + kTicketBytes;
+constexpr size_t kStaticBytes = static_cast<size_t>(48) << 20;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
+static __device__ uint32_t g_static_err;  // zero at load; see SampleArgs::epoch
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
+void* g_err_addr[kMaxDevices] = {};
+uint32_t g_epoch[kMaxDevices] = {};
 
 // Rows the stream kernel does not own (general rows) keep this status.
 __global__ void mark_unhandled_kernel(int rows, int32_t* out_token, int32_t* out_status) {
@@ -52,15 +51,22 @@ __global__ void mark_unhandled_kernel(int rows, int32_t* out_token, int32_t* out
 // Device address of g_static_scratch on the current device. In host code the
 // symbol names a host-side stand-in, not device memory, so the address is
 // looked up once per device (with that device current) and cached.
-cudaError_t static_scratch(int device, void** out) {
+// Also hands out the call's epoch (never 0).
+cudaError_t static_scratch(int device, void** out, uint32_t** err, uint32_t* epoch) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_scratch_addr[device] == nullptr) {
         void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        void* eptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&eptr, g_static_err);
         if (e != cudaSuccess) return e;
         g_scratch_addr[device] = ptr;
+        g_err_addr[device] = eptr;
     }
     *out = g_scratch_addr[device];
+    *err = static_cast<uint32_t*>(g_err_addr[device]);
+    if (++g_epoch[device] == 0u) g_epoch[device] = 1u;
+    *epoch = g_epoch[device];
     return cudaSuccess;
 }
 
@@ -80,18 +86,18 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     if (vocab == 0 || !logits_dev || !params_dev || !out_token_dev || !out_status_dev ||
         (!uniforms_dev && !rng_state_dev) || (hist_off_dev && !hist_dev))
         return TQFS_ERR_INVALID_ARG;
-    const Plan plan = plan_stream(vocab);
-    if (rows > kStaticRows || static_cast<long long>(rows) * plan.slices > kStaticPairs ||
-        plan.slices > 64)
+    const Plan plan = plan_stream(rows, vocab, dtype);
+    if (plan.chunks == 0 || stream_scratch(rows, plan, nullptr, nullptr) > kStaticBytes)
         return TQFS_ERR_UNSUPPORTED;  // beyond the fixed scratch: use tqfs_sample
     int device = -1;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
         return TQFS_ERR_NO_DEVICE;
     void* base = nullptr;
-    if (static_scratch(device, &base) != cudaSuccess) return TQFS_ERR_CUDA;
+    uint32_t* err = nullptr;
+    uint32_t epoch = 0;
+    if (static_scratch(device, &base, &err, &epoch) != cudaSuccess) return TQFS_ERR_CUDA;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned char* b = static_cast<unsigned char*>(base);
     SampleArgs a{};
     a.logits = logits_dev;
     a.dtype = dtype;
@@ -105,19 +111,14 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     a.rng_state = rng_state_dev;
     a.out_token = out_token_dev;
     a.out_status = out_status_dev;
-    a.cand = reinterpret_cast<unsigned long long*>(b);
-    a.cand_n = reinterpret_cast<int*>(b + kCandBytes);
-    a.top4 = reinterpret_cast<unsigned long long*>(b + kCandBytes + kCountBytes);
-    a.ticket = reinterpret_cast<unsigned int*>(b + kCandBytes + kCountBytes + kTop4Bytes);
-    a.slices = plan.slices;
-    a.slice_len = plan.slice_len;
+    stream_scratch(rows, plan, base, &a);
+    a.err_word = err;
+    a.epoch = epoch;
     const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = (reinterpret_cast<uintptr_t>(logits_dev) & 15u) == 0 &&
                (static_cast<size_t>(ld) * esz) % 16 == 0;
     a.top4_only = 0;
 
-    if (cudaMemsetAsync(a.ticket, 0, static_cast<size_t>(rows) * 4, s) != cudaSuccess)
-        return TQFS_ERR_CUDA;
     mark_unhandled_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token_dev, out_status_dev);
     if (cudaGetLastError() != cudaSuccess) return TQFS_ERR_CUDA;
     return launch_stream(a, plan, s) == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;

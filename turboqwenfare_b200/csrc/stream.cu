@@ -1,29 +1,43 @@
-// Stream kernel: one pass over every logits row for greedy rows and for rows
-// whose top_k is in [1, kMaxK] and below the vocabulary (the reference's
-// common configurations). The last CTA of a row to finish finalises it.
+// Stream path of tqfs_sample: greedy rows and sampled rows with
+// 0 < top_k <= kStreamMaxK (row_mode in common.cuh). Three kernels per call:
 //
-// Work layout. A row is split into `slices` contiguous id ranges of
-// `slice_len` ids; CTA (row, slice) streams its range from HBM exactly once
-// into registers (16-byte evict-first loads, 40 logits per thread) and then:
-//   1. builds a shared-memory table of the slice's penalised logits: the
-//      row's window (src/sampling/mod.rs:114-148) is counted with atomics and
-//      each repeated id's value is penalised once, so the per-element work is
-//      a table load and a select (no division in the streaming loop);
-//   2. keeps the greedy top-4 of the raw logits (src/runtime/decode.rs:
-//      48-64) when the row is greedy or diagnostics are requested;
-//   3. for sampled rows, selects its local top-k by (value desc, id asc):
-//      theta = k-th largest per-thread maximum is a lower bound of the local
-//      k-th value (k distinct elements reach it), so comparing the registers
-//      against it yields a short candidate list (about k entries) that is
-//      ranked in shared memory; a bisection over the key space replaces the
-//      estimate when the list overflows;
-//   4. writes its sorted local list to scratch and takes a ticket. The CTA
-//      that takes the last ticket merges the row's lists (every global top-k
-//      member is in its slice's local top-k), then runs softmax, top_p, min_p
-//      and the inverse-CDF draw over the k survivors exactly as
-//      src/sampling/mod.rs:166-248 does, with the sequential f32 sums done
-//      in the reference's order by one thread.
-// No CTA ever waits for another: the ticket is a fetch-add after a fence.
+// window_kernel (only when a history is given): one CTA per penalised row
+//   buckets the row's penalty window (the last min(repeat_last_n, len)
+//   tokens, src/sampling/mod.rs:114-148) by chunk and counts each distinct
+//   id (the reference's count map, mod.rs:127-132), so a chunk later reads
+//   only the (id, count) pairs that fall inside it.
+//
+// stream_kernel: every logits row is cut into chunks of 2,048 ids (8 KiB of
+//   f32, 4 KiB of bf16) and a (row, chunk) pair is a work item, taken in
+//   runs of consecutive chunks of one row (units). The grid is persistent
+//   and every warp owns a fixed sequence of units; there is no block-wide
+//   barrier. Each warp keeps two chunk buffers in shared memory: while it
+//   works on one chunk (held in registers, 64 f32 values per lane), a bulk
+//   copy (cp.async.bulk, one instruction, no multicast) fills the other with
+//   its next chunk. Per chunk the warp
+//     1. keeps the greedy top-4 of the raw logits (src/runtime/decode.rs:
+//        48-64) for greedy rows, or when diagnostics are requested;
+//     2. penalises (mod.rs:139-146) the chunk's window ids, one lane per id,
+//        in shared memory, and reloads its registers;
+//     3. finds theta, an order value that at least k of its elements reach:
+//        the lane's ids are split into G groups (G = 1, 2, 4 for k <= 32, 64,
+//        128); a group's ceil(k/G)-th largest lane maximum is reached by that
+//        many distinct elements, so the smallest of the G is reached by k;
+//     4. writes the keys of the elements at or above theta (which contain the
+//        chunk's top-k by (value desc, id asc)) and theta itself. When more
+//        than max(2k, 64) elements reach theta it is first raised by
+//        bisection over the order values, keeping the count >= k; exact ties
+//        at the final value are resolved to the lowest ids.
+//
+// finalize_kernel: one CTA per row. Every chunk's theta is a lower bound of
+//   the row's k-th value, so the largest of them filters the candidate lists;
+//   the survivors are sorted, and softmax, top_p, min_p and the inverse-CDF
+//   draw run over the k survivors exactly as src/sampling/mod.rs:166-248 does
+//   (sequential f32 sums in order, by one thread).
+//
+// No kernel waits on another CTA or on a flag. The only waits are on a
+// warp's own bulk copies; each gives up after 2 s, sets the call's error word
+// and the rows report TQFS_ROW_ERR_TIMEOUT.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -35,27 +49,20 @@ namespace tqfs {
 
 namespace {
 
-constexpr uint32_t kNoPenalty = 0xFFFFFFFFu;  // table sentinel: GPU arithmetic never
-                                              // produces this NaN pattern
-
-struct Fixed {
-    float wsort[kThreads];               // per-warp sorted thread maxima
-    unsigned long long topk[kMaxK];      // merged top-k keys, then probability keys
-    unsigned long long pkey[kMaxK];
-    float e[kMaxK];
-    float prob[kMaxK];                   // probabilities in draw order
-    unsigned long long wtop4[kWarps][4];
-    unsigned long long top4[4];
-    float theta;
-    int theta_found;
-    int off[65];
-    int ncand;
-    int cnt[kWarps];
-    int last;
-    int err;
-    float total;
-    int result[2];
-};
+constexpr int kSW = 8;            // warps per CTA of the stream kernel
+constexpr int kST = kSW * 32;
+constexpr int kSlots = 16;        // float4 register slots per lane per chunk
+constexpr int kChunkLen = kSlots * 32 * 4;  // 2,048 ids per chunk
+constexpr int kListCap = 384;     // keys of a warp's candidate list
+constexpr int kListOff = 16384;   // per-warp shared memory: chunk buffers (+ exchange),
+constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins
+constexpr int kWarpSmem = kBinsOff + 256 * 4;      // 20 KiB
+constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
+constexpr int kFT = 256;          // threads per finalize CTA
+constexpr int kFW = kFT / 32;
+constexpr int kSurvCap = 8192;    // survivors the finaliser selects from in shared memory
+constexpr int kWinWarps = 8;      // warps of the window kernel
+constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
 
 __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned long long k) {
     if (k <= t[3]) return;
@@ -76,7 +83,7 @@ __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned lo
     }
 }
 
-// Warp-wide top-4 of the lanes' sorted top-4 lists (4 extraction rounds).
+// Warp-wide top-4 of the lanes' descending top-4 lists (4 extraction rounds).
 __device__ __forceinline__ void warp_top4(unsigned long long t[4], unsigned long long out[4],
                                           int lane) {
 #pragma unroll
@@ -93,9 +100,9 @@ __device__ __forceinline__ void warp_top4(unsigned long long t[4], unsigned long
     }
 }
 
-// Per-thread top-4 of raw logits by strict '>' (src/runtime/decode.rs:48-64):
-// elements arrive in increasing id order per thread, so among equal values
-// the earlier id keeps its place; NaN and -inf never enter.
+// Per-lane top-4 of raw logits by strict '>' (src/runtime/decode.rs:48-64):
+// a lane sees its ids in increasing order, so among equal values the earlier
+// id keeps its place; NaN and -inf never enter.
 struct Top4 {
     float v0 = -INFINITY, v1 = -INFINITY, v2 = -INFINITY, v3 = -INFINITY;
     int i0 = 0, i1 = 0, i2 = 0, i3 = 0;
@@ -133,15 +140,9 @@ struct Top4 {
     }
 };
 
-// Entries > x in a descending array.
-__device__ __forceinline__ int count_greater(const unsigned long long* arr, int n,
-                                             unsigned long long x) {
-    int lo = 0, hi = n;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (arr[mid] > x) lo = mid + 1; else hi = mid;
-    }
-    return lo;
+__device__ __noinline__ Top4 top4_insert_slow(Top4 t, float x, int id) {
+    t.insert(x, id);
+    return t;
 }
 
 __device__ __forceinline__ float warp_sort_desc_f(float x, int lane) {
@@ -158,411 +159,841 @@ __device__ __forceinline__ float warp_sort_desc_f(float x, int lane) {
     return x;
 }
 
-template <int DT>
-struct Elem;
-template <>
-struct Elem<0> {
-    static constexpr int kVec = 4;
-    static constexpr int kSize = 4;
-    __device__ static float get(const uint4& r, int i) { return __uint_as_float((&r.x)[i]); }
-    __device__ static void put(uint4& r, int i, const unsigned char* p) {
-        (&r.x)[i] = *reinterpret_cast<const unsigned int*>(p);
-    }
-    __device__ static float load(const unsigned char* rowp, int e) {
-        return reinterpret_cast<const float*>(rowp)[e];
-    }
-};
-template <>
-struct Elem<1> {
-    static constexpr int kVec = 8;
-    static constexpr int kSize = 2;
-    __device__ static float get(const uint4& r, int i) {
-        const unsigned w = (&r.x)[i >> 1];
-        return bf16_bits_to_f32((i & 1) ? (w >> 16) : (w & 0xFFFFu));
-    }
-    __device__ static void put(uint4& r, int i, const unsigned char* p) {
-        const unsigned h = *reinterpret_cast<const unsigned short*>(p);
-        unsigned& w = (&r.x)[i >> 1];
-        w = (i & 1) ? ((w & 0xFFFFu) | (h << 16)) : ((w & 0xFFFF0000u) | h);
-    }
-    __device__ static float load(const unsigned char* rowp, int e) {
-        return bf16_bits_to_f32(reinterpret_cast<const unsigned short*>(rowp)[e]);
-    }
-};
-
-// Exact k-th largest key of the slice (values staged in shared memory), by
-// bisection over the 64-bit key space. Out of line: only the overflow
-// fallback (many equal values, or k close to kMaxK) reaches it.
-__device__ __noinline__ unsigned long long bisect_kth(const float* staged, int n, int lo,
-                                                      unsigned int k, int* cnt) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    unsigned long long blo = 1ull, bhi = ~0ull;
-    while (blo < bhi) {
-        const unsigned long long mid = blo + ((bhi - blo) >> 1) + 1ull;
-        int c = 0;
-        for (int i = tid; i < n; i += kThreads)
-            c += make_key(order32(staged[i]), static_cast<uint32_t>(lo + i)) >= mid;
-        c = warp_sum(c);
-        __syncthreads();
-        if (lane == 0) cnt[warp] = c;
-        __syncthreads();
-        int s = 0;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += cnt[w];
-        if (s >= static_cast<int>(k)) blo = mid; else bhi = mid - 1ull;
-    }
-    return blo;
+// The rank-th largest (0-based) of the lanes' values.
+__device__ __forceinline__ float warp_rank_value(float x, int rank, int lane) {
+    return __shfl_sync(0xFFFFFFFFu, warp_sort_desc_f(x, lane), rank);
 }
 
-template <int DT, bool TOP4>
-__global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
-    using E = Elem<DT>;
-    constexpr int VEC = E::kVec;
-    constexpr int NCH = kElemsPerThread / VEC;
+__device__ __forceinline__ int warp_excl_scan(int x, int lane) {
+    int incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    return incl - x;
+}
+
+// A chunk lands in its warp's buffer in id order: 2,048 f32 or bf16 values.
+template <int DT>
+struct Raw {
+    static constexpr int kES = DT == 0 ? 4 : 2;   // element bytes
+    static constexpr int kBuf = kChunkLen * kES;  // bytes of a chunk buffer
+};
+
+struct Pen {
+    float rep, freq, pres;
+};
+
+// What a warp knows about an item before touching its logits. Lanes 0..9
+// load the row's tqfs_params words, lanes 10..13 the history offsets and the
+// chunk's window entry range; decode() gathers them with shuffles.
+//
+// Work layout: a unit is a run of up to unit_len consecutive chunks of one
+// row; units are numbered unit-major (unit i is unit i / rows of row
+// i % rows) and warp w of nw takes units w, w + nw, ... A position is
+// (unit, chunk of the row).
+struct Pos {
+    int row;
+    int u;      // unit of the row; the position is valid while u < units
+    int chunk;  // chunk of the row
+};
+
+// A position's work. Row fields (mode .. pn) come from the row's params and
+// history offsets and are decoded once per unit; the window range per chunk.
+struct Info {
+    int mode;  // -1: past the end
+    int row;
+    int u;
+    int chunk;
+    bool last;  // last chunk of its unit
+    int k;
+    bool unit_pen;  // the row has a non-empty penalty window
+    bool pen;       // ... with ids in this chunk
+    Pen pn;
+    uint32_t w0, w1;  // window entries [w0, w1) of this chunk
+};
+
+// Next position of a warp whose unit stride is nw_u units of a row plus
+// nw_row rows.
+__device__ __forceinline__ Pos next_pos(const SampleArgs& a, Pos p, int nw_row, int nw_u) {
+    const int end = min(a.chunks, (p.u + 1) * a.unit_len);
+    if (p.chunk + 1 < end) return Pos{p.row, p.u, p.chunk + 1};
+    Pos q;
+    q.row = p.row + nw_row;
+    q.u = p.u + nw_u;
+    if (q.row >= a.rows) {
+        q.row -= a.rows;
+        ++q.u;
+    }
+    q.chunk = q.u * a.unit_len;
+    return q;
+}
+
+// Lanes 0..9 load the row's tqfs_params words and lanes 10..11 its history
+// offsets (skipped within a unit), lanes 12..13 the chunk's window range.
+__device__ __forceinline__ unsigned long long info_word(const SampleArgs& a, Pos p, bool same_unit,
+                                                        int lane) {
+    if (p.u >= a.units) return 0ull;
+    if (lane < 12) {
+        if (same_unit || a.top4_only) return 0ull;
+        if (lane < 10) return __ldg(reinterpret_cast<const unsigned int*>(a.params + p.row) + lane);
+        if (a.hist_off == nullptr) return 0ull;
+        return static_cast<unsigned long long>(__ldg(a.hist_off + p.row + (lane - 10)));
+    }
+    if (lane > 13 || a.hist_off == nullptr || a.top4_only) return 0ull;
+    return __ldcg(a.win_off + (static_cast<size_t>(p.row) * a.chunks + p.chunk) * 2 + (lane - 12));
+}
+
+__device__ __forceinline__ bool same_unit(Pos p, const Info& prev) {
+    return prev.mode != -1 && p.row == prev.row && p.u == prev.u;
+}
+
+__device__ __forceinline__ Info decode(unsigned long long w, Pos p, const Info& prev,
+                                       const SampleArgs& a) {
+    Info f;
+    f.w0 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 12));
+    f.w1 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 13));
+    if (p.u >= a.units) {
+        f.mode = -1;
+        return f;
+    }
+    if (same_unit(p, prev)) {
+        f = prev;
+        f.w0 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 12));
+        f.w1 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 13));
+    } else {
+        unsigned int pw[10];
+#pragma unroll
+        for (int i = 0; i < 10; ++i)
+            pw[i] = static_cast<unsigned int>(__shfl_sync(0xFFFFFFFFu, w, i));
+        const long long hs = static_cast<long long>(__shfl_sync(0xFFFFFFFFu, w, 10));
+        const long long he = static_cast<long long>(__shfl_sync(0xFFFFFFFFu, w, 11));
+        tqfs_params prm;
+        static_assert(sizeof(tqfs_params) == 40, "tqfs_params layout");
+        memcpy(&prm, pw, sizeof(prm));
+        long long ws, wl;
+        f.mode = row_mode(prm, hs, he, a.hist_off != nullptr, a.vocab, a.top4_only != 0, &ws, &wl);
+        f.k = static_cast<int>(prm.top_k);
+        f.unit_pen = f.mode == kModeStream && wl > 0;
+        f.pn = Pen{prm.repeat_penalty, prm.frequency_penalty, prm.presence_penalty};
+        f.row = p.row;
+        f.u = p.u;
+    }
+    f.chunk = p.chunk;
+    f.last = p.chunk + 1 >= min(a.chunks, (p.u + 1) * a.unit_len);
+    f.pen = f.unit_pen && f.w1 > f.w0;
+    return f;
+}
+
+__device__ __forceinline__ unsigned long long warp_min64(unsigned long long x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = umin64(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+    return x;
+}
+
+// Keeps the min(n, k) largest of the n distinct keys L[0..n) in L[0..),
+// in any order, and returns the smallest kept key (0 when n == 0). Radix
+// select over 8-bit digits with a per-warp histogram in `bins`.
+__device__ __noinline__ unsigned long long warp_keep_top(unsigned long long* L, int* n_io, int k,
+                                                         unsigned int* bins) {
+    const int lane = threadIdx.x & 31;
+    const int n = *n_io;
+    if (n <= k) {
+        unsigned long long mn = ~0ull;
+        for (int i = lane; i < n; i += 32) mn = umin64(mn, L[i]);
+        mn = warp_min64(mn);
+        return n > 0 ? mn : 0ull;
+    }
+    unsigned long long prefix = 0ull;
+    int remaining = k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bins[lane * 8 + i] = 0u;
+        __syncwarp();
+        const unsigned long long hmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
+        for (int i = lane; i < n; i += 32) {
+            const unsigned long long key = L[i];
+            if ((key & hmask) == prefix) atomicAdd(&bins[static_cast<int>((key >> shift) & 255u)], 1u);
+        }
+        __syncwarp();
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum += static_cast<int>(bins[255 - 8 * lane - i]);
+        const int above = warp_excl_scan(sum, lane);
+        const bool mine = above < remaining && remaining <= above + sum;
+        int d = 0, ab = 0, cd = 0;
+        if (mine) {
+            int c = above;
+            for (int i = 0; i < 8; ++i) {
+                const int dd = 255 - 8 * lane - i;
+                const int h = static_cast<int>(bins[dd]);
+                if (c + h >= remaining) {
+                    d = dd;
+                    ab = c;
+                    cd = h;
+                    break;
+                }
+                c += h;
+            }
+        }
+        const int src = __ffs(__ballot_sync(0xFFFFFFFFu, mine)) - 1;
+        d = __shfl_sync(0xFFFFFFFFu, d, src);
+        ab = __shfl_sync(0xFFFFFFFFu, ab, src);
+        cd = __shfl_sync(0xFFFFFFFFu, cd, src);
+        prefix |= static_cast<unsigned long long>(d) << shift;
+        remaining -= ab;
+        __syncwarp();
+        if (cd == remaining) {  // every key under the prefix is kept: take their minimum
+            const unsigned long long pmask = ~0ull << shift;
+            unsigned long long mn = ~0ull;
+            for (int i = lane; i < n; i += 32) {
+                const unsigned long long key = L[i];
+                if ((key & pmask) == prefix) mn = umin64(mn, key);
+            }
+            prefix = warp_min64(mn);
+            break;
+        }
+    }
+    const unsigned long long kth = prefix;
+    int base = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const unsigned long long key = i < n ? L[i] : 0ull;
+        const bool keep = i < n && key >= kth;
+        const unsigned ball = __ballot_sync(0xFFFFFFFFu, keep);
+        __syncwarp();
+        if (keep) L[base + __popc(ball & ((1u << lane) - 1u))] = key;
+        base += __popc(ball);
+        __syncwarp();
+    }
+    *n_io = base;
+    return kth;
+}
+
+// The chunk's values from shared memory by id: f32, or bf16 widened.
+template <bool F32>
+__device__ __forceinline__ float chunk_value(const void* v, int id) {
+    if constexpr (F32) return static_cast<const float*>(v)[id];
+    else return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(v)[id]) << 16);
+}
+
+// Appends to `out` (room for kChunkCap keys) a set of the chunk's keys that
+// contains its top-k by (value desc, id asc), and returns how many:
+//   theta = an order value k ids reach: the lane's ids (id = t*32 + lane) are
+//   split into G groups by t & (G-1) (G = 1, 2, 4 for k <= 32, 64, 128); a
+//   group's ceil(k/G)-th largest lane maximum is reached by that many
+//   distinct ids, so the smallest of the G is reached by k;
+//   while more than max(2k, 64) ids reach it, it is raised by bisection over
+//   the order values keeping the count >= k; exact ties at the final value
+//   are resolved to the lowest ids.
+template <bool F32>
+__device__ __noinline__ int chunk_select(const void* vals, int n_here, int base_id, int k,
+                                         unsigned long long* out, int* counter) {
+    const int lane = threadIdx.x & 31;
+    const int nt = (n_here + 31) / 32;
+    float g[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int t = 0; t < nt; ++t) {
+        const int id = t * 32 + lane;
+        if (id < n_here) g[t & 3] = fmaxf(g[t & 3], chunk_value<F32>(vals, id));
+    }
+    const float lane_max = fmaxf(fmaxf(g[0], g[1]), fmaxf(g[2], g[3]));
+    float theta;
+    if (k <= 32) {
+        theta = warp_rank_value(lane_max, k - 1, lane);
+    } else if (k <= 64) {
+        const int r = (k + 1) / 2 - 1;
+        theta = fminf(warp_rank_value(fmaxf(g[0], g[2]), r, lane),
+                      warp_rank_value(fmaxf(g[1], g[3]), r, lane));
+    } else {
+        const int r = (k + 3) / 4 - 1;
+        theta = fminf(fminf(warp_rank_value(g[0], r, lane), warp_rank_value(g[1], r, lane)),
+                      fminf(warp_rank_value(g[2], r, lane), warp_rank_value(g[3], r, lane)));
+    }
+    // ids whose order value reaches t (t == 0: every id, NaN included)
+    auto count_ge = [&](uint32_t t) {
+        const float f = ord_threshold(t);
+        int c = 0;
+        for (int s = 0; s < nt; ++s) {
+            const int id = s * 32 + lane;
+            if (id < n_here) c += (t == 0u) || (chunk_value<F32>(vals, id) >= f);
+        }
+        return warp_sum(c);
+    };
+    auto write_ge = [&](uint32_t t, int limit) {
+        if (lane == 0) *counter = 0;
+        __syncwarp();
+        const float f = ord_threshold(t);
+        for (int s = 0; s < nt; ++s) {
+            const int id = s * 32 + lane;
+            if (id < n_here) {
+                const float v = chunk_value<F32>(vals, id);
+                if ((t == 0u) || v >= f) {
+                    const int pos = atomicAdd(counter, 1);
+                    if (pos < limit) out[pos] = make_key(order32(v), static_cast<uint32_t>(base_id + id));
+                }
+            }
+        }
+        __syncwarp();
+        return *counter;
+    };
+    const int tgt = max(2 * k, 64);  // <= kChunkCap
+    const uint32_t t0 = order32(theta);  // theta is never NaN
+    int c = write_ge(t0, kChunkCap);
+    if (c >= k && c <= tgt) return c;
+    // bisection between tlo (reached by >= k) and thi (reached by < k)
+    float cmax = lane_max;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xFFFFFFFFu, cmax, o));
+    uint32_t tlo = 0u, thi = order32(cmax) + 1u;
+    int c_lo = -1, c_hi = 0;
+    uint32_t probe = t0;
+    for (;;) {
+        if (c >= k || probe == 0u) {
+            tlo = probe;
+            c_lo = c;
+        } else {
+            thi = probe;
+            c_hi = c;
+        }
+        if (c_lo < 0) {
+            probe = 0u;
+        } else {
+            if (c_lo <= tgt || thi - tlo <= 1u) break;
+            probe = tlo + (thi - tlo) / 2u;
+        }
+        c = count_ge(probe);
+    }
+    if (c_lo <= tgt) return write_ge(tlo, kChunkCap);
+    // ties at tlo (thi == tlo + 1): every id reaching thi, then the lowest
+    // ids at tlo up to k
+    write_ge(thi, kChunkCap);
+    const int need = k - c_hi;
+    int run = 0;
+    for (int s = 0; s < nt && run < need; ++s) {
+        const int id = s * 32 + lane;
+        const bool tie = id < n_here && order32(chunk_value<F32>(vals, id)) == tlo;
+        const unsigned ball = __ballot_sync(0xFFFFFFFFu, tie);
+        const int idx = run + __popc(ball & ((1u << lane) - 1u));
+        if (tie && idx < need) out[c_hi + idx] = make_key(tlo, static_cast<uint32_t>(base_id + id));
+        run += __popc(ball);
+    }
+    __syncwarp();
+    return k;
+}
+
+// Penalised value of one window id (mod.rs:139-146); out of line so the
+// many call sites stay small.
+__device__ __noinline__ float penalise_id(float v, uint32_t count, float rep, float freq, float pres) {
+    return penalise(v, count, rep, freq, pres);
+}
+
+// Per-lane maxima of the chunk's values (NaN ignored) by slot: a slot is 4
+// f32 ids, (j*32 + lane)*4 + 0..3, or 8 bf16 ids, (j*32 + lane)*8 + 0..7
+// (bf16 uses slots 0..7). Ids at or beyond n_here are left out.
+template <bool F32>
+__device__ __forceinline__ void slot_maxima(const void* vals, int n_here, int lane, float (&sm)[kSlots]) {
+    constexpr int PER = F32 ? 4 : 8;
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) sm[j] = -INFINITY;
+    if (n_here == kChunkLen) {
+        if constexpr (F32) {
+            const float4* p = static_cast<const float4*>(vals);
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) {
+                const float4 v = p[j * 32 + lane];
+                sm[j] = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+            }
+        } else {
+            const uint4* p = static_cast<const uint4*>(vals);
+#pragma unroll
+            for (int j = 0; j < kSlots / 2; ++j) {
+                const uint4 u = p[j * 32 + lane];
+                const float a0 = fmaxf(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u));
+                const float a1 = fmaxf(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+                const float a2 = fmaxf(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u));
+                const float a3 = fmaxf(__uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
+                sm[j] = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) {
+            const int e0 = (j * 32 + lane) * PER;
+            if (F32 || j < kSlots / 2)
+                for (int q = 0; q < PER; ++q)
+                    if (e0 + q < n_here) sm[j] = fmaxf(sm[j], chunk_value<F32>(vals, e0 + q));
+        }
+    }
+}
+
+// Appends the keys of the ids of this lane's slots in `mask` whose value
+// beats thr (v > thr, or v >= thr with `incl`); positions come from *counter
+// and only those below room are written.
+template <bool F32>
+__device__ __noinline__ void insert_slots(const void* vals, unsigned mask, int n_here, float thr,
+                                          bool incl, int base_id, unsigned long long* out,
+                                          int* counter, int room) {
+    constexpr int PER = F32 ? 4 : 8;
+    const int lane = threadIdx.x & 31;
+    while (mask != 0u) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        const int e0 = (j * 32 + lane) * PER;
+        for (int q = 0; q < PER; ++q) {
+            const int id = e0 + q;
+            if (id < n_here) {
+                const float v = chunk_value<F32>(vals, id);
+                if (v > thr || (incl && v == thr)) {
+                    const int pos = atomicAdd(counter, 1);
+                    if (pos < room) out[pos] = make_key(order32(v), static_cast<uint32_t>(base_id + id));
+                }
+            }
+        }
+    }
+}
+
+// One chunk of a unit. With `sel` (the unit's exact k-th value th is known)
+// it appends the ids that beat th: ids only grow along a unit, so a later id
+// at the k-th value ranks below it and strict '>' is exact. Without it (the
+// unit's first chunk) it appends the ids at or above theta, an order value
+// that k of them reach: the lane's slots are split into G groups (G = 1, 2, 4
+// for k <= 32, 64, 128) and a group's ceil(k/G)-th largest lane maximum is
+// reached by that many distinct ids, so the smallest of the G is reached by
+// k. Returns the number appended; -1 when the chunk needs the full selection
+// (too many ids reach theta, or fewer than k do).
+template <bool F32>
+__device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel, float th, int k,
+                                          int base_id, unsigned long long* out, int* counter,
+                                          int room) {
+    const int lane = threadIdx.x & 31;
+    float sm[kSlots];
+    slot_maxima<F32>(vals, n_here, lane, sm);
+    float thr = th;
+    if (!sel) {
+        float g[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) g[j & 3] = fmaxf(g[j & 3], sm[j]);
+        const float lane_max = fmaxf(fmaxf(g[0], g[1]), fmaxf(g[2], g[3]));
+        if (k <= 32) {
+            thr = warp_rank_value(lane_max, k - 1, lane);
+        } else if (k <= 64) {
+            const int r = (k + 1) / 2 - 1;
+            thr = fminf(warp_rank_value(fmaxf(g[0], g[2]), r, lane),
+                        warp_rank_value(fmaxf(g[1], g[3]), r, lane));
+        } else {
+            const int r = (k + 3) / 4 - 1;
+            thr = fminf(fminf(warp_rank_value(g[0], r, lane), warp_rank_value(g[1], r, lane)),
+                        fminf(warp_rank_value(g[2], r, lane), warp_rank_value(g[3], r, lane)));
+        }
+        if (!(thr > -INFINITY)) return -1;  // too few numbers: select in full
+    }
+    unsigned mask = 0u;
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j)
+        mask |= static_cast<unsigned>(sel ? sm[j] > thr : sm[j] >= thr) << j;
+    if (!__any_sync(0xFFFFFFFFu, mask != 0u)) return 0;
+    if (lane == 0) *counter = 0;
+    __syncwarp();
+    if (mask != 0u) insert_slots<F32>(vals, mask, n_here, thr, !sel, base_id, out, counter, room);
+    __syncwarp();
+    const int c = *counter;
+    if (!sel && (c > room || c < k)) return -1;
+    return c;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_diag) {
+    constexpr int ES = Raw<DT>::kES;
     extern __shared__ __align__(16) unsigned char dyn[];
-    __shared__ Fixed fx;
+    __shared__ int wcount[kSW];
+    __shared__ __align__(8) unsigned long long wbar[kSW][2];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    // This warp's area: two chunk buffers, for bf16 an f32 exchange area (f32
+    // chunks are penalised in their own buffer), the candidate list, bins.
+    unsigned char* wbase = dyn + static_cast<size_t>(warp) * kWarpSmem;
+    float* xch = reinterpret_cast<float*>(wbase + 2 * Raw<DT>::kBuf);
+    unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase + kListOff);
+    unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + kBinsOff);
+    if (lane == 0) {
+        mbar_init(&wbar[warp][0], 1);
+        mbar_init(&wbar[warp][1], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
 
-    const int row = blockIdx.x / a.slices;
-    const int slice = blockIdx.x - row * a.slices;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = static_cast<int>(gridDim.x) * kSW;
+    const int nw_row = nw % a.rows, nw_u = nw / a.rows;
+    const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
 
-    const tqfs_params p = a.params ? a.params[row] : tqfs_params{};
-    const bool greedy = a.top4_only || p.temperature == 0.0f;
-    const uint32_t k = p.top_k;
-    const bool smallk = !greedy && k != 0u && k < static_cast<uint32_t>(a.vocab) &&
-                        k <= static_cast<uint32_t>(kMaxK);
-    if (!greedy && !smallk) return;  // general rows are another kernel's
-    const bool want_top4 = greedy || a.out_top4 != nullptr;
-    const bool pen = !greedy && !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f &&
-                                  p.presence_penalty == 0.0f);
-    const int lo = slice * a.slice_len;
-    const int hi = min(lo + a.slice_len, a.vocab);
-    const int n_here = hi - lo;
-    const int nchunks = (n_here + VEC - 1) / VEC;
-
-    // ---- 1. stream this slice into registers ------------------------------
-    const unsigned char* rowp =
-        static_cast<const unsigned char*>(a.logits) + static_cast<size_t>(row) * a.ld * E::kSize;
-    uint4 raw[NCH];
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-        raw[j] = make_uint4(0u, 0u, 0u, 0u);
-        const int c = tid + j * kThreads;
-        if (c < nchunks) {
-            const int e0 = lo + c * VEC;
-            if (a.vec_ok && e0 + VEC <= hi) {
-                raw[j] = ld_stream16(rowp + static_cast<size_t>(e0) * E::kSize);
-            } else {
-#pragma unroll
-                for (int i = 0; i < VEC; ++i)
-                    if (e0 + i < hi) E::put(raw[j], i, rowp + static_cast<size_t>(e0 + i) * E::kSize);
-            }
+    auto chunk_len = [&](const Info& f) {
+        const int lo = f.chunk * kChunkLen;
+        return a.vocab - lo < kChunkLen ? a.vocab - lo : kChunkLen;
+    };
+    // Buffer bi receives the item's chunk: one bulk copy of its 16-byte
+    // multiple (lane 0), plain copies of anything else (unaligned rows or a
+    // ragged tail). Every item, copied or not, completes one barrier phase.
+    auto start_copy = [&](const Info& f, int bi) {
+        unsigned char* buf = wbase + bi * Raw<DT>::kBuf;
+        const bool copy = f.mode == kModeGreedy || f.mode == kModeStream;
+        const unsigned char* src = nullptr;
+        int bytes = 0;
+        uint32_t bulk = 0u;
+        if (copy) {
+            src = logits +
+                  (static_cast<size_t>(f.row) * a.ld + static_cast<size_t>(f.chunk) * kChunkLen) * ES;
+            bytes = chunk_len(f) * ES;
+            bulk = a.vec_ok ? static_cast<uint32_t>(bytes) & ~15u : 0u;
         }
-    }
-
-    // ---- 2. penalised-value table (overlaps the loads in flight) ----------
-    uint32_t* table = reinterpret_cast<uint32_t*>(dyn);
-    long long wstart = 0, wlen = 0;
-    if (pen && a.hist_off != nullptr) {
-        const long long hs = a.hist_off[row], he = a.hist_off[row + 1];
-        const unsigned long long len = he > hs ? static_cast<unsigned long long>(he - hs) : 0ull;
-        const unsigned long long w = p.repeat_last_n < len ? p.repeat_last_n : len;
-        wlen = static_cast<long long>(w);
-        wstart = he - wlen;
-    }
-    const bool use_table = wlen > 0;
-    if (tid == 0) {
-        fx.err = 0;
-        fx.theta_found = 0;
-        fx.ncand = 0;
-    }
-    if (use_table) {
-        uint4* t4 = reinterpret_cast<uint4*>(table);
-        for (int i = tid; i < (a.slice_len >> 2); i += kThreads)
-            t4[i] = make_uint4(kNoPenalty, kNoPenalty, kNoPenalty, kNoPenalty);
-        __syncthreads();
-        // Counting from the sentinel: the first increment wraps it to 0, so an
-        // entry holds count - 1. The occurrence that performs the first
-        // increment lists the id, so each repeated id is penalised once.
-        int* firsts = reinterpret_cast<int*>(dyn + static_cast<size_t>(a.slice_len) * 4);
-        for (long long j = tid; j < wlen; j += kThreads) {
-            const int t = a.hist[wstart + j];
-            if (t >= lo && t < hi) {
-                if (atomicAdd(table + (t - lo), 1u) == kNoPenalty) {
-                    const int idx = atomicAdd(&fx.ncand, 1);
-                    if (idx < kFirstsCap) firsts[idx] = t - lo;
-                }
-            }
-        }
-        __syncthreads();
-        const int nfirst = fx.ncand;
-        if (nfirst <= kFirstsCap) {
-            for (int q = tid; q < nfirst; q += kThreads) {
-                const int i = firsts[q];
-                const float v = E::load(rowp, lo + i);
-                table[i] = __float_as_uint(penalise(v, table[i] + 1u, p.repeat_penalty,
-                                                    p.frequency_penalty, p.presence_penalty));
-            }
-        } else {  // more distinct ids than the list holds: scan the table
-            for (int i = tid; i < n_here; i += kThreads) {
-                const uint32_t cm1 = table[i];
-                if (cm1 != kNoPenalty) {
-                    const float v = E::load(rowp, lo + i);
-                    table[i] = __float_as_uint(penalise(v, cm1 + 1u, p.repeat_penalty,
-                                                        p.frequency_penalty, p.presence_penalty));
-                }
-            }
-        }
-        __syncthreads();
-        if (tid == 0) fx.ncand = 0;
-    }
-
-    // ---- 3. widen, greedy top-4 of raw logits, penalised values, max ------
-    float vals[kElemsPerThread];
-    Top4 t4;
-    float tmax = -INFINITY;
-    if (greedy) {
-        // Greedy rows: only the top-4 of the raw logits (no table, no filter).
-#pragma unroll
-        for (int j = 0; j < NCH; ++j) {
-            const int c = tid + j * kThreads;
-            const int e0 = lo + c * VEC;
-            if (c < nchunks) {
-#pragma unroll
-                for (int i = 0; i < VEC; ++i)
-                    if (e0 + i < hi) t4.insert(E::get(raw[j], i), e0 + i);
-            }
-        }
-    }
-    if (!greedy) {
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-        const int c = tid + j * kThreads;
-        const int e0 = lo + c * VEC;
-        float v[VEC];
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) v[i] = E::get(raw[j], i);
-        if (e0 + VEC > hi) {  // the slice's last, partial chunk (or none)
-#pragma unroll
-            for (int i = 0; i < VEC; ++i)
-                if (e0 + i >= hi) v[i] = __uint_as_float(0x7FC00000u);  // NaN: never selected
-        }
-        if (c < nchunks) {
-            if constexpr (TOP4) {
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) t4.insert(v[i], e0 + i);
-            }
-            if (use_table) {
-                uint32_t tb[VEC];
-                const uint4 w0 = *reinterpret_cast<const uint4*>(table + (e0 - lo));
-                tb[0] = w0.x;
-                tb[1] = w0.y;
-                tb[2] = w0.z;
-                tb[3] = w0.w;
-                if constexpr (VEC == 8) {
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(table + (e0 - lo) + 4);
-                    tb[4] = w1.x;
-                    tb[5] = w1.y;
-                    tb[6] = w1.z;
-                    tb[7] = w1.w;
-                }
-#pragma unroll
-                for (int i = 0; i < VEC; ++i)
-                    if (tb[i] != kNoPenalty) v[i] = __uint_as_float(tb[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-            vals[j * VEC + i] = v[i];
-            tmax = fmaxf(tmax, v[i]);
-        }
-    }
-    }
-
-    const size_t ls = static_cast<size_t>(row) * a.slices + slice;
-    if (want_top4) {
-        unsigned long long t4k[4];
-        t4.keys(t4k);
-        unsigned long long wt[4];
-        warp_top4(t4k, wt, lane);
         if (lane == 0) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) fx.wtop4[warp][r] = wt[r];
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&wbar[warp][bi], bulk);
+            if (bulk != 0u) bulk_load(buf, src, bulk, &wbar[warp][bi]);
         }
-    }
-
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(
-        dyn + static_cast<size_t>(a.slice_len) * 4);
-    int nloc = 0;
-    if (smallk) {
-        // ---- 4. theta = k-th largest thread maximum -----------------------
-        fx.wsort[warp * 32 + lane] = warp_sort_desc_f(tmax, lane);
-        __syncthreads();
-        if (k <= 32u) {
-            // One warp merges the 8 sorted lists by extraction: k rounds.
-            if (warp == 0) {
-                int ptr = 0;
-                float head = lane < kWarps ? fx.wsort[lane * 32] : __uint_as_float(0x7FC00000u);
-                float kth = -INFINITY;
-                for (uint32_t r = 0; r < k; ++r) {
-                    float m = head;
+        for (int i = static_cast<int>(bulk) / ES + lane; i < bytes / ES; i += 32) {
+            if constexpr (DT == 0)
+                reinterpret_cast<unsigned int*>(buf)[i] = __ldcs(reinterpret_cast<const unsigned int*>(src) + i);
+            else
+                reinterpret_cast<unsigned short*>(buf)[i] = __ldcs(reinterpret_cast<const unsigned short*>(src) + i);
+        }
+    };
+    auto load_entries = [&](const Info& f, uint32_t (&en)[4]) {
 #pragma unroll
-                    for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-                    m = __shfl_sync(0xFFFFFFFFu, m, 0);
-                    const unsigned ball = __ballot_sync(0xFFFFFFFFu, lane < kWarps && head == m);
-                    if (ball != 0u && lane == __ffs(ball) - 1) {
-                        ++ptr;
-                        head = ptr < 32 ? fx.wsort[lane * 32 + ptr] : __uint_as_float(0x7FC00000u);
-                    }
-                    kth = m;
-                }
+        for (int m = 0; m < 4; ++m) en[m] = 0u;
+        if (!f.pen) return;
+        const uint32_t* src = a.win_ent + static_cast<size_t>(f.row) * kWinCap + f.w0;
+        const int ne = static_cast<int>(f.w1 - f.w0);
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+            if (lane + 32 * m < ne) en[m] = __ldcg(src + lane + 32 * m);
+    };
+
+    // Warps are numbered across CTAs first, so consecutive units land on
+    // different SMs. Prologue: positions p0 (cur) and p1 (nxt) are being
+    // copied; the words of p2 are in flight.
+    const int gw = warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+    Pos p0;
+    p0.row = gw % a.rows;
+    p0.u = gw / a.rows;
+    p0.chunk = p0.u * a.unit_len;
+    const Pos p1 = next_pos(a, p0, nw_row, nw_u);
+    Pos p2 = next_pos(a, p1, nw_row, nw_u);
+    Info none;
+    none.mode = -1;
+    Info cur = decode(info_word(a, p0, false, lane), p0, none, a);
+    Info nxt = decode(info_word(a, p1, same_unit(p1, cur), lane), p1, cur, a);
+    unsigned long long w2 = info_word(a, p2, same_unit(p2, nxt), lane);
+    start_copy(cur, 0);
+    start_copy(nxt, 1);
+    uint32_t en[4];
+    load_entries(cur, en);
+    int b = 0;
+    uint32_t parity = 0u;  // bit bi: parity of buffer bi's next phase
+
+    // Unit state: the candidate list L[0..n) holds keys whose top-k is the
+    // top-k of the unit so far; with `sel`, L is exactly that top-k and
+    // th_ord the order value of its smallest key.
+    int n = 0;
+    bool sel = false;
+    uint32_t th_ord = 0u;
+    Top4 t4;
+
+#pragma unroll 1
+    while (cur.mode != -1) {
+        const Info nn = decode(w2, p2, nxt, a);
+        p2 = next_pos(a, p2, nw_row, nw_u);
+        w2 = info_word(a, p2, same_unit(p2, nn), lane);
+        uint32_t enn[4];
+        load_entries(nxt, enn);
+        {
+            const bool ok = mbar_wait_bounded(&wbar[warp][b], (parity >> b) & 1u, kWaitBudgetNs);
+            parity ^= 1u << b;
+            if (!__all_sync(0xFFFFFFFFu, ok)) {
+                // A copy did not land in time: report it, wait (bounded) for
+                // the other buffer's copy so none lands after exit, and stop.
                 if (lane == 0) {
-                    fx.theta = kth;
-                    fx.theta_found = kth == kth;
+                    atomicMax(a.err_word, a.epoch);
+                    mbar_wait_bounded(&wbar[warp][b ^ 1], (parity >> (b ^ 1)) & 1u, kWaitBudgetNs);
                 }
-            }
-        } else {
-            int gt = 0, ge = 0;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const float* s = fx.wsort + w * 32;
-                int l0 = 0, h0 = 32, l1 = 0, h1 = 32;
-                while (l0 < h0) {
-                    const int m = (l0 + h0) >> 1;
-                    if (s[m] > tmax) l0 = m + 1; else h0 = m;
-                }
-                while (l1 < h1) {
-                    const int m = (l1 + h1) >> 1;
-                    if (s[m] >= tmax) l1 = m + 1; else h1 = m;
-                }
-                gt += l0;
-                ge += l1;
-            }
-            if (gt < static_cast<int>(k) && static_cast<int>(k) <= ge) {
-                fx.theta = tmax;  // every writer holds the same value
-                fx.theta_found = 1;
+                __syncwarp();
+                return;
             }
         }
-        __syncthreads();
-        const float theta = fx.theta;
-        const bool take_all = !fx.theta_found || !(theta > -INFINITY);
-        // ---- 5. filter ----------------------------------------------------
-        if (!take_all) {
-#pragma unroll
-            for (int j = 0; j < NCH; ++j) {
-                float cm = vals[j * VEC];
-#pragma unroll
-                for (int i = 1; i < VEC; ++i) cm = fmaxf(cm, vals[j * VEC + i]);
-                if (cm >= theta) {
-                    const int e0 = lo + (tid + j * kThreads) * VEC;
-#pragma unroll
-                    for (int i = 0; i < VEC; ++i) {
-                        if (vals[j * VEC + i] >= theta) {
-                            const int idx = atomicAdd(&fx.ncand, 1);
-                            if (idx < kCandCap)
-                                cand[idx] = make_key(order32(vals[j * VEC + i]),
-                                                     static_cast<uint32_t>(e0 + i));
-                        }
-                    }
-                }
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < NCH; ++j) {
-                const int e0 = lo + (tid + j * kThreads) * VEC;
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) {
-                    if (e0 + i < hi) {
-                        const int idx = atomicAdd(&fx.ncand, 1);
-                        if (idx < kCandCap)
-                            cand[idx] = make_key(order32(vals[j * VEC + i]),
-                                                 static_cast<uint32_t>(e0 + i));
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        if (fx.ncand > kCandCap) {
-            // Overflow: stage the penalised values and bisect for the exact
-            // local k-th key, then keep exactly the keys >= it.
-            float* staged = reinterpret_cast<float*>(dyn);
-#pragma unroll
-            for (int j = 0; j < NCH; ++j) {
-                const int e0 = (tid + j * kThreads) * VEC;
-#pragma unroll
-                for (int i = 0; i < VEC; ++i)
-                    if (e0 + i < n_here) staged[e0 + i] = vals[j * VEC + i];
-            }
-            __syncthreads();
-            const unsigned long long kth = bisect_kth(staged, n_here, lo, k, fx.cnt);
-            __syncthreads();
-            if (tid == 0) fx.ncand = 0;
-            __syncthreads();
-#pragma unroll
-            for (int j = 0; j < NCH; ++j) {
-                const int e0 = lo + (tid + j * kThreads) * VEC;
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) {
-                    if (e0 + i < hi) {
-                        const unsigned long long key =
-                            make_key(order32(vals[j * VEC + i]), static_cast<uint32_t>(e0 + i));
-                        if (key >= kth) {
-                            const int idx = atomicAdd(&fx.ncand, 1);
-                            if (idx < kCandCap) cand[idx] = key;
-                        }
-                    }
-                }
-            }
-            __syncthreads();
-        }
-        nloc = min(fx.ncand, kCandCap);
-        // ---- 6. rank the candidates, keep the local top-k -----------------
-        unsigned long long* out = a.cand + ls * kMaxK;
-        for (int idx = tid; idx < nloc; idx += kThreads) {
-            const unsigned long long key = cand[idx];
-            int r = 0;
-            for (int q = 0; q < nloc; ++q) r += cand[q] > key;
-            if (r < static_cast<int>(k)) out[r] = key;
-        }
-        nloc = min(nloc, static_cast<int>(k));
-    }
-    __syncthreads();
-    if (tid == 0) {
-        if (smallk) a.cand_n[ls] = fx.err ? -1 : nloc;
-        if (want_top4) {
-            unsigned long long m[4] = {0ull, 0ull, 0ull, 0ull};
-            for (int w = 0; w < kWarps; ++w)
-                for (int r = 0; r < 4; ++r) top4_insert(m, fx.wtop4[w][r]);
-            for (int r = 0; r < 4; ++r) a.top4[ls * 4 + r] = m[r];
-        }
-    }
-    if (a.out_probs != nullptr && !a.top4_only) {
-        float* pr = a.out_probs + static_cast<size_t>(row) * a.ld;
-        for (int e = lo + tid; e < hi; e += kThreads) pr[e] = 0.0f;
-    }
+        __syncwarp();
 
-    // ---- 7. ticket: the last CTA of the row finalises ----------------------
-    __threadfence();
+        if (cur.mode == kModeGreedy || cur.mode == kModeStream) {
+            const int base_id = cur.chunk * kChunkLen;
+            const int n_here = chunk_len(cur);
+            const size_t uslot = static_cast<size_t>(cur.row) * a.units + cur.u;
+            const bool greedy = cur.mode == kModeGreedy;
+            unsigned char* buf = wbase + b * Raw<DT>::kBuf;
+
+            // ---- 1. greedy top-4 of the raw logits (kept over the unit) ----
+            // A lane takes ids lane, lane + 32, ...: increasing, as the
+            // strict '>' tie rule needs.
+            if (greedy || top4_diag) {
+                for (int id = lane; id < n_here; id += 32) {
+                    const float v = chunk_value<DT == 0>(buf, id);
+                    if (v > t4.v3) t4 = top4_insert_slow(t4, v, base_id + id);
+                }
+                if (cur.last) {
+                    unsigned long long k4[4], o4[4];
+                    t4.keys(k4);
+                    warp_top4(k4, o4, lane);
+                    if (lane == 0) {
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) a.top4[uslot * 4 + r] = o4[r];
+                    }
+                    t4 = Top4();
+                }
+            }
+            if (a.out_probs != nullptr) {
+                float* pr = a.out_probs + static_cast<size_t>(cur.row) * a.ld + base_id;
+                for (int e = lane; e < n_here; e += 32) pr[e] = 0.0f;
+            }
+
+            if (!greedy) {
+                const int k = cur.k;
+                // ---- 2. penalties: one lane per distinct window id ----------
+                // Values by id: the chunk's own buffer (f32 penalised in
+                // place), or the f32 exchange area (bf16 widened first).
+                const void* vals = buf;
+                bool vals_f32 = DT == 0;
+                if (cur.pen) {
+                    float* f = reinterpret_cast<float*>(buf);
+                    if (DT == 1) {
+                        f = xch;
+                        const uint4* p = reinterpret_cast<const uint4*>(buf);
+#pragma unroll
+                        for (int j = 0; j < kSlots / 2; ++j) {
+                            const uint4 u = p[j * 32 + lane];
+                            float4* d = reinterpret_cast<float4*>(f + (j * 32 + lane) * 8);
+                            d[0] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                               __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+                            d[1] = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u),
+                                               __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
+                        }
+                        __syncwarp();
+                    }
+                    const int ne = static_cast<int>(cur.w1 - cur.w0);
+                    const uint32_t* src = a.win_ent + static_cast<size_t>(cur.row) * kWinCap + cur.w0;
+                    for (int i = lane; i < ne; i += 32) {
+                        const uint32_t e = i < 32 ? en[0]
+                                         : i < 64 ? en[1]
+                                         : i < 96 ? en[2]
+                                         : i < 128 ? en[3] : __ldcg(src + i);
+                        const uint32_t id = e >> 16;
+                        f[id] = penalise_id(f[id], e & 0xFFFFu, cur.pn.rep, cur.pn.freq, cur.pn.pres);
+                    }
+                    __syncwarp();
+                    vals = f;
+                    vals_f32 = true;
+                }
+
+                // ---- 3. the chunk's candidates, appended to L -------------
+                const int room = kListCap - n;
+                const float th = sel ? from_order32(th_ord) : 0.0f;
+                int c = vals_f32
+                            ? unit_chunk<true>(vals, n_here, sel, th, k, base_id, L + n, &wcount[warp], room)
+                            : unit_chunk<false>(vals, n_here, sel, th, k, base_id, L + n, &wcount[warp], room);
+                bool full = !sel;
+                if (c >= 0 && !(sel && c > room)) {
+                    n += c;
+                } else {
+                    // ---- 4. the full selection (overflow, ties, NaN) --------
+                    // The partial appends are dropped; L keeps room for it.
+                    full = true;
+                    if (n > k) warp_keep_top(L, &n, k, bins);
+                    c = vals_f32 ? chunk_select<true>(vals, n_here, base_id, k, L + n, &wcount[warp])
+                                 : chunk_select<false>(vals, n_here, base_id, k, L + n, &wcount[warp]);
+                    n += c;
+                }
+                // ---- 5. keep L short; with k keys it defines the unit's k-th
+                if (full ? n >= k : n > kListCap - kChunkCap) {
+                    const unsigned long long kth = warp_keep_top(L, &n, k, bins);
+                    th_ord = static_cast<uint32_t>(kth >> 32);
+                    sel = n >= k && th_ord != 0u;  // a NaN k-th admits every number
+                }
+                // ---- 6. unit end: its exact top-k and its k-th value -------
+                if (cur.last) {
+                    const unsigned long long kth = warp_keep_top(L, &n, k, bins);
+                    unsigned long long* dst = a.cand + uslot * kUnitCap;
+                    for (int i = lane; i < n; i += 32) dst[i] = L[i];
+                    if (lane == 0) {
+                        a.cand_n[uslot] = n;
+                        a.theta[uslot] = n >= k ? static_cast<uint32_t>(kth >> 32) : 0u;
+                    }
+                    __syncwarp();
+                    n = 0;
+                    sel = false;
+                    th_ord = 0u;
+                }
+            }
+        }
+        // Every value of the buffer has been read: refill it.
+        __syncwarp();
+        start_copy(nn, b);
+
+        // ---- rotate -------------------------------------------------------
+#pragma unroll
+        for (int m = 0; m < 4; ++m) en[m] = enn[m];
+        cur = nxt;
+        nxt = nn;
+        b ^= 1;
+    }
+}
+
+// Buckets the penalty window of every stream-sampled row by chunk and counts
+// each distinct id: win_ent holds, per chunk, (id - chunk start) << 16 | count
+// for every distinct id of the chunk, win_off the [start, end) of each chunk's
+// entries. Ids outside [0, vocab) are dropped, as the reference's count map
+// never meets them among the candidates (mod.rs:139).
+__global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
+    extern __shared__ __align__(16) unsigned char wdyn[];
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(wdyn);  // kMaxChunks + 1
+    uint32_t* start = cnt + kMaxChunks + 1;               // kMaxChunks + 1
+    uint32_t* tbl = start + kMaxChunks + 1;               // kWinWarps x kChunkLen/2
+    uint16_t* buf = reinterpret_cast<uint16_t*>(tbl + kWinWarps * (kChunkLen / 2));  // kWinCap
+    __shared__ uint32_t nd[kWinWarps];
+    const int row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NT = kWinWarps * 32;
+    const tqfs_params p = a.params[row];
+    const long long hs = a.hist_off[row], he = a.hist_off[row + 1];
+    long long ws, wl;
+    if (row_mode(p, hs, he, true, a.vocab, false, &ws, &wl) != kModeStream) return;
+    const int C = a.chunks;
+    uint32_t* off = a.win_off + static_cast<size_t>(row) * C * 2;
+    if (wl == 0) {
+        for (int i = tid; i < 2 * C; i += NT) off[i] = 0u;
+        return;
+    }
+    for (int i = tid; i <= C; i += NT) cnt[i] = 0u;
+    for (int i = tid; i < kWinWarps * (kChunkLen / 2); i += NT) tbl[i] = 0u;
     __syncthreads();
-    if (tid == 0) {
-        const unsigned int t = atomicAdd(&a.ticket[row], 1u);
-        fx.last = (t == static_cast<unsigned int>(a.slices - 1)) ? 1 : 0;
+    const int32_t* src = a.hist + ws;
+    const int n = static_cast<int>(wl);  // <= kWinCap
+    constexpr int PER = kWinCap / NT;
+    int tok[PER];
+#pragma unroll
+    for (int m = 0; m < PER; ++m) {
+        const int j = tid + m * NT;
+        tok[m] = j < n ? src[j] : -1;
+    }
+#pragma unroll
+    for (int m = 0; m < PER; ++m)
+        if (tok[m] >= 0 && tok[m] < a.vocab) atomicAdd(&cnt[tok[m] / kChunkLen], 1u);
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the C bucket sizes
+        const int per = (C + 31) / 32;
+        const int b0 = lane * per;
+        uint32_t s = 0;
+        for (int i = 0; i < per; ++i)
+            if (b0 + i < C) s += cnt[b0 + i];
+        uint32_t run = static_cast<uint32_t>(warp_excl_scan(static_cast<int>(s), lane));
+        for (int i = 0; i < per; ++i) {
+            if (b0 + i < C) {
+                const uint32_t x = cnt[b0 + i];
+                cnt[b0 + i] = run;
+                start[b0 + i] = run;
+                run += x;
+            }
+        }
+        if (lane == 31) start[C] = run;
     }
     __syncthreads();
-    if (!fx.last) return;
-    __threadfence();
+#pragma unroll
+    for (int m = 0; m < PER; ++m) {
+        const int t = tok[m];
+        if (t >= 0 && t < a.vocab) {
+            const int c = t / kChunkLen;
+            buf[atomicAdd(&cnt[c], 1u)] = static_cast<uint16_t>(t - c * kChunkLen);
+        }
+    }
+    __syncthreads();
+    // Per chunk: count into this warp's 16-bit table, then the lane that
+    // clears an id's count emits (id, count) once, leaving the table clean.
+    uint32_t* wt = tbl + warp * (kChunkLen / 2);
+    uint32_t* ent = a.win_ent + static_cast<size_t>(row) * kWinCap;
+    for (int c = warp; c < C; c += kWinWarps) {
+        const uint32_t s0 = start[c], s1 = start[c + 1];
+        if (lane == 0) nd[warp] = 0u;
+        __syncwarp();
+        for (uint32_t i = s0 + lane; i < s1; i += 32) {
+            const uint32_t t = buf[i];
+            atomicAdd(&wt[t >> 1], 1u << (16 * (t & 1u)));
+        }
+        __syncwarp();
+        for (uint32_t i = s0 + lane; i < s1; i += 32) {
+            const uint32_t t = buf[i];
+            const uint32_t sh = 16 * (t & 1u);
+            const uint32_t old = atomicAnd(&wt[t >> 1], ~(0xFFFFu << sh));
+            const uint32_t count = (old >> sh) & 0xFFFFu;
+            if (count != 0u) ent[s0 + atomicAdd(&nd[warp], 1u)] = (t << 16) | count;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            off[2 * c] = s0;
+            off[2 * c + 1] = s0 + nd[warp];
+        }
+        __syncwarp();
+    }
+}
 
+struct FinalShared {
+    unsigned long long topk[kStreamMaxK];  // top-k keys, then probability keys
+    unsigned long long pkey[kStreamMaxK];
+    float e[kStreamMaxK];
+    float prob[kStreamMaxK];               // probabilities in draw order
+    unsigned long long w4[kFW][4];
+    unsigned long long top4[4];
+    int noff[kMaxChunks + 1];              // prefix of the units' list lengths
+    uint32_t wmax[kFW];
+    unsigned int hist[256];                // radix-select digit counts
+    unsigned long long wcnt;
+    int n;
+    int rdig, rabove;
+    float total;
+    int result[2];
+};
+
+// One CTA per row: merges the units' lists written by stream_kernel and
+// finalises the row (greedy: top-4; sampled: exact top-k, softmax, top_p,
+// min_p, draw as src/sampling/mod.rs:166-248).
+__global__ void __launch_bounds__(kFT) finalize_kernel(SampleArgs a) {
+    extern __shared__ __align__(16) unsigned char fdyn[];
+    __shared__ FinalShared fs;
+    unsigned long long* g = reinterpret_cast<unsigned long long*>(fdyn);  // kSurvCap keys
+    const int row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const tqfs_params p = a.top4_only ? tqfs_params{} : a.params[row];
+    long long hs = 0, he = 0;
+    if (a.hist_off != nullptr && !a.top4_only) {
+        hs = a.hist_off[row];
+        he = a.hist_off[row + 1];
+    }
+    long long ws, wl;
+    const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab, a.top4_only != 0, &ws, &wl);
+    if (mode == kModeGeneral) return;  // the general kernel's row
+    const bool greedy = mode == kModeGreedy;
+    const int C = a.units;
+    const size_t base = static_cast<size_t>(row) * C;
     int token = 0;
-    unsigned long long* g = reinterpret_cast<unsigned long long*>(dyn);
-    if (want_top4) {
-        const int n4 = a.slices * 4;
-        for (int i = tid; i < n4; i += kThreads)
-            g[i] = __ldcg(a.top4 + static_cast<size_t>(row) * a.slices * 4 + i);
+
+    if (greedy || a.out_top4 != nullptr) {
+        unsigned long long t[4] = {0ull, 0ull, 0ull, 0ull};
+        for (int i = tid; i < C * 4; i += kFT) top4_insert(t, __ldcg(a.top4 + base * 4 + i));
+        unsigned long long o[4];
+        warp_top4(t, o, lane);
+        if (lane == 0)
+            for (int r = 0; r < 4; ++r) fs.w4[warp][r] = o[r];
         __syncthreads();
         if (tid == 0) {
             unsigned long long m[4] = {0ull, 0ull, 0ull, 0ull};
-            for (int i = 0; i < n4; ++i) top4_insert(m, g[i]);
-            for (int r = 0; r < 4; ++r) fx.top4[r] = m[r];
+            for (int w = 0; w < kFW; ++w)
+                for (int r = 0; r < 4; ++r) top4_insert(m, fs.w4[w][r]);
+            for (int r = 0; r < 4; ++r) fs.top4[r] = m[r];
             if (a.out_top4 != nullptr) {
                 for (int r = 0; r < 4; ++r) {
                     tqfs_candidate cnd;
@@ -573,84 +1004,203 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
             }
         }
         __syncthreads();
-        token = fx.top4[0] ? static_cast<int>(key_token(fx.top4[0])) : 0;
+        token = fs.top4[0] ? static_cast<int>(key_token(fs.top4[0])) : 0;
     }
 
-    int status = TQFS_ROW_OK;
-    if (smallk) {
-        // ---- 8. merge the slices' sorted lists into the row's top-k -------
-        if (tid < a.slices)
-            fx.off[tid + 1] = __ldcg(a.cand_n + static_cast<size_t>(row) * a.slices + tid);
-        __syncthreads();
+    if (!greedy) {
+        const int k = static_cast<int>(p.top_k);
+        // ---- list lengths (prefix) and the row bound -----------------------
+        uint32_t tb = 0u;
+        for (int c = tid; c < C; c += kFT) {
+            fs.noff[c + 1] = __ldcg(a.cand_n + base + c);
+            tb = max(tb, __ldcg(a.theta + base + c));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tb = max(tb, __shfl_xor_sync(0xFFFFFFFFu, tb, o));
+        if (lane == 0) fs.wmax[warp] = tb;
         if (tid == 0) {
-            int acc = 0;
-            fx.off[0] = 0;
-            for (int s = 0; s < a.slices; ++s) {
-                const int n = fx.off[s + 1];
-                if (n < 0) fx.err = 1;
-                acc += n > 0 ? n : 0;
-                fx.off[s + 1] = acc;
+            fs.noff[0] = 0;
+            fs.n = 0;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const int per = (C + 31) / 32;
+            const int b0 = lane * per;
+            int s = 0;
+            for (int i = 0; i < per; ++i)
+                if (b0 + i < C) s += fs.noff[b0 + i + 1];
+            int run = warp_excl_scan(s, lane);
+            for (int i = 0; i < per; ++i) {
+                if (b0 + i < C) {
+                    run += fs.noff[b0 + i + 1];
+                    fs.noff[b0 + i + 1] = run;
+                }
+            }
+        }
+        tb = 0u;
+        for (int w = 0; w < kFW; ++w) tb = max(tb, fs.wmax[w]);
+        __syncthreads();
+        const unsigned long long kb = static_cast<unsigned long long>(tb) << 32;
+        const int total_n = fs.noff[C];
+        // ---- gather the survivors: entry q of the concatenated lists -------
+        for (int q0 = 0; q0 < total_n; q0 += kFT * 4) {
+            unsigned long long key[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * kFT + tid;
+                key[u] = 0ull;
+                if (q < total_n) {
+                    int lo = 0, hi = C;  // the chunk c with noff[c] <= q < noff[c+1]
+                    while (hi - lo > 1) {
+                        const int mid = (lo + hi) >> 1;
+                        if (fs.noff[mid] <= q) lo = mid; else hi = mid;
+                    }
+                    key[u] = __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo]));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (q0 + u * kFT + tid < total_n && key[u] >= kb) {
+                    const int idx = atomicAdd(&fs.n, 1);
+                    if (idx < kSurvCap) g[idx] = key[u];
+                }
             }
         }
         __syncthreads();
-        const int total_n = fx.off[a.slices];
-        for (int s = 0; s < a.slices; ++s) {
-            const int n = fx.off[s + 1] - fx.off[s];
-            const unsigned long long* src =
-                a.cand + (static_cast<size_t>(row) * a.slices + s) * kMaxK;
-            for (int i = tid; i < n; i += kThreads) g[fx.off[s] + i] = __ldcg(src + i);
+        int m = fs.n;
+        if (m > kSurvCap) {
+            // Rare (heavy ties): the exact k-th key by bisection over the
+            // lists, then exactly the k keys at or above it.
+            unsigned long long kth = 0ull;
+            for (int bit = 63; bit >= 0; --bit) {
+                const unsigned long long cand = kth | (1ull << bit);
+                unsigned long long cnt = 0ull;
+                for (int q = tid; q < total_n; q += kFT) {
+                    int lo = 0, hi = C;
+                    while (hi - lo > 1) {
+                        const int mid = (lo + hi) >> 1;
+                        if (fs.noff[mid] <= q) lo = mid; else hi = mid;
+                    }
+                    cnt += __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo])) >= cand;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+                if (tid == 0) fs.wcnt = 0ull;
+                __syncthreads();
+                if (lane == 0) atomicAdd(&fs.wcnt, cnt);
+                __syncthreads();
+                if (fs.wcnt >= static_cast<unsigned long long>(k)) kth = cand;
+                __syncthreads();
+            }
+            if (tid == 0) fs.n = 0;
+            __syncthreads();
+            for (int q = tid; q < total_n; q += kFT) {
+                int lo = 0, hi = C;
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (fs.noff[mid] <= q) lo = mid; else hi = mid;
+                }
+                const unsigned long long key =
+                    __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo]));
+                if (key >= kth) g[atomicAdd(&fs.n, 1)] = key;
+            }
+            __syncthreads();
+            m = fs.n;
+        }
+        // ---- the k-th largest survivor key (radix select, 8-bit digits) ----
+        unsigned long long kth = 0ull;
+        if (m > k) {
+            int remaining = k;
+            for (int shift = 56; shift >= 0; shift -= 8) {
+                for (int i = tid; i < 256; i += kFT) fs.hist[i] = 0u;
+                __syncthreads();
+                const unsigned long long hmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
+                for (int i = tid; i < m; i += kFT) {
+                    const unsigned long long key = g[i];
+                    if ((key & hmask) == kth)
+                        atomicAdd(&fs.hist[static_cast<int>((key >> shift) & 255u)], 1u);
+                }
+                __syncthreads();
+                if (warp == 0) {
+                    // lane l covers digits 255 - 8l down to 248 - 8l
+                    int sum = 0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) sum += static_cast<int>(fs.hist[255 - 8 * lane - i]);
+                    const int above = warp_excl_scan(sum, lane);
+                    if (above < remaining && remaining <= above + sum) {
+                        int c = above;
+                        for (int i = 0; i < 8; ++i) {
+                            const int d = 255 - 8 * lane - i;
+                            const int h = static_cast<int>(fs.hist[d]);
+                            if (c + h >= remaining) {
+                                fs.rdig = d;
+                                fs.rabove = c;
+                                break;
+                            }
+                            c += h;
+                        }
+                    }
+                }
+                __syncthreads();
+                kth |= static_cast<unsigned long long>(fs.rdig) << shift;
+                remaining -= fs.rabove;
+                __syncthreads();
+            }
+        }
+        // ---- the top-k keys, ranked by (value desc, id asc) -----------------
+        const int kk = min(k, m);
+        if (tid == 0) fs.n = 0;
+        __syncthreads();
+        for (int i = tid; i < m; i += kFT) {
+            const unsigned long long key = g[i];
+            if (key >= kth) fs.pkey[atomicAdd(&fs.n, 1)] = key;
         }
         __syncthreads();
-        for (int idx = tid; idx < total_n; idx += kThreads) {
-            int s = 0;
-            while (fx.off[s + 1] <= idx) ++s;
-            const unsigned long long x = g[idx];
-            int r = idx - fx.off[s];
-            for (int s2 = 0; s2 < a.slices && r < static_cast<int>(k); ++s2)
-                if (s2 != s) r += count_greater(g + fx.off[s2], fx.off[s2 + 1] - fx.off[s2], x);
-            if (r < static_cast<int>(k)) fx.topk[r] = x;
+        if (tid < kk) {
+            const unsigned long long key = fs.pkey[tid];
+            int r = 0;
+            for (int q = 0; q < kk; ++q) r += fs.pkey[q] > key;
+            fs.topk[r] = key;
         }
         __syncthreads();
-        const int kk = min(static_cast<int>(k), total_n);
-
-        // ---- 9. softmax over the survivors (src/sampling/mod.rs:166-190) --
-        const float first = kk > 0 ? key_value(fx.topk[0]) : 0.0f;
+        // softmax over the survivors (src/sampling/mod.rs:166-190)
+        const float first = kk > 0 ? key_value(fs.topk[0]) : 0.0f;
         const float mx = (kk > 0 && first == first) ? first : -INFINITY;
         if (tid < kk) {
-            const float v = key_value(fx.topk[tid]);
-            fx.e[tid] = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
+            const float v = key_value(fs.topk[tid]);
+            fs.e[tid] = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
         }
         __syncthreads();
         if (tid == 0) {
             float total = -0.0f;
-            for (int i = 0; i < kk; ++i) total = __fadd_rn(total, fx.e[i]);
-            fx.total = total;
+            for (int i = 0; i < kk; ++i) total = __fadd_rn(total, fs.e[i]);
+            fs.total = total;
         }
         __syncthreads();
-        const float total = fx.total;
+        const float total = fs.total;
         float pv = 0.0f;
         unsigned long long pk = 0ull;
         if (tid < kk) {
-            pv = total > 0.0f ? __fdiv_rn(fx.e[tid], total) : fx.e[tid];
-            pk = make_key(order32(pv), key_token(fx.topk[tid]));
-            fx.pkey[tid] = pk;
+            pv = total > 0.0f ? __fdiv_rn(fs.e[tid], total) : fs.e[tid];
+            pk = make_key(order32(pv), key_token(fs.topk[tid]));
+            fs.pkey[tid] = pk;
         }
         __syncthreads();
         if (tid < kk) {
             int r = 0;
-            for (int q = 0; q < kk; ++q) r += fx.pkey[q] > pk;
-            fx.topk[r] = pk;  // probability keys in draw order
-            fx.prob[r] = pv;
+            for (int q = 0; q < kk; ++q) r += fs.pkey[q] > pk;
+            fs.topk[r] = pk;  // probability keys in draw order
+            fs.prob[r] = pv;
         }
         __syncthreads();
-        // ---- 10. top_p, min_p, draw (src/sampling/mod.rs:195-248) ---------
+        // top_p, min_p, draw (src/sampling/mod.rs:195-248)
         if (tid == 0) {
             int keep = kk;
             if (!(p.top_p >= 1.0f)) {
                 float cum = 0.0f;
                 int n = 0;
                 for (int i = 0; i < kk; ++i) {
-                    cum = __fadd_rn(cum, fx.prob[i]);
+                    cum = __fadd_rn(cum, fs.prob[i]);
                     ++n;
                     if (cum >= p.top_p) break;
                 }
@@ -658,54 +1208,53 @@ __global__ void __launch_bounds__(kThreads, 3) stream_kernel(SampleArgs a) {
                 if (keep > kk) keep = kk;
             }
             if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
-                const float floor = __fmul_rn(p.min_p, fx.prob[0]);
+                const float floor = __fmul_rn(p.min_p, fs.prob[0]);
                 int n = 0;
-                while (n < keep && fx.prob[n] >= floor) ++n;
+                while (n < keep && fs.prob[n] >= floor) ++n;
                 keep = n < 1 ? 1 : n;
             }
             int tok = 0;
             if (keep > 0) {
                 int pick = 0;
                 float total2 = -0.0f;
-                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, fx.prob[i]);
+                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, fs.prob[i]);
                 if (isfinite(total2) && total2 > 0.0f) {
                     float u;
                     if (a.uniforms != nullptr) {
                         u = a.uniforms[row];
                     } else {
-                        uint64_t s[4];
-                        uint64_t* st = a.rng_state + static_cast<size_t>(row) * 4;
-                        for (int q = 0; q < 4; ++q) s[q] = st[q];
-                        u = xoshiro_next_f32(s);
-                        for (int q = 0; q < 4; ++q) st[q] = s[q];
+                        uint64_t st[4];
+                        uint64_t* sp = a.rng_state + static_cast<size_t>(row) * 4;
+                        for (int q = 0; q < 4; ++q) st[q] = sp[q];
+                        u = xoshiro_next_f32(st);
+                        for (int q = 0; q < 4; ++q) sp[q] = st[q];
                     }
                     const float target = __fmul_rn(u, total2);
                     float cum = 0.0f;
                     pick = keep - 1;
                     for (int i = 0; i < keep; ++i) {
-                        cum = __fadd_rn(cum, fx.prob[i]);
+                        cum = __fadd_rn(cum, fs.prob[i]);
                         if (cum >= target) {
                             pick = i;
                             break;
                         }
                     }
                 }
-                tok = static_cast<int>(key_token(fx.topk[pick]));
+                tok = static_cast<int>(key_token(fs.topk[pick]));
             }
-            fx.result[0] = tok;
-            fx.result[1] = keep;
+            fs.result[0] = tok;
+            fs.result[1] = keep;
         }
         __syncthreads();
-        token = fx.result[0];
-        const int keep = fx.result[1];
+        token = fs.result[0];
+        const int keep = fs.result[1];
         if (a.out_probs != nullptr && tid < keep)
-            a.out_probs[static_cast<size_t>(row) * a.ld + key_token(fx.topk[tid])] = fx.prob[tid];
-        if (fx.err) status = TQFS_ROW_ERR_WINDOW;
+            a.out_probs[static_cast<size_t>(row) * a.ld + key_token(fs.topk[tid])] = fs.prob[tid];
     }
     if (tid == 0) {
-        if (a.out_token != nullptr) a.out_token[row] = token;
-        if (a.out_status != nullptr) a.out_status[row] = status;
-        a.ticket[row] = 0u;  // ready for the next launch
+        const bool timed_out = a.err_word != nullptr && *a.err_word == a.epoch;
+        if (a.out_token != nullptr) a.out_token[row] = timed_out ? -1 : token;
+        if (a.out_status != nullptr) a.out_status[row] = timed_out ? TQFS_ROW_ERR_TIMEOUT : TQFS_ROW_OK;
     }
 }
 
@@ -719,31 +1268,119 @@ __global__ void fill_empty_kernel(int rows, int32_t* out_token, int32_t* out_sta
         for (int i = 0; i < 4; ++i) out_top4[static_cast<size_t>(r) * 4 + i] = tqfs_candidate{0u, -INFINITY};
 }
 
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+constexpr size_t kWindowSmem = static_cast<size_t>(2 * (kMaxChunks + 1)) * 4 +
+                               static_cast<size_t>(kWinWarps) * (kChunkLen / 2) * 4 +
+                               static_cast<size_t>(kWinCap) * 2;
+
 }  // namespace
 
-Plan plan_stream(int vocab) {
+Plan plan_stream(int rows, int vocab, int dtype) {
     Plan pl;
-    pl.slices = (vocab + kMaxSliceLen - 1) / kMaxSliceLen;
-    if (pl.slices < 1) pl.slices = 1;
-    const int per = (vocab + pl.slices - 1) / pl.slices;
-    pl.slice_len = (per + 7) & ~7;
-    const size_t work = static_cast<size_t>(pl.slice_len) * 4 + static_cast<size_t>(kCandCap) * 8;
-    const size_t gather = static_cast<size_t>(pl.slices) * kMaxK * 8;
-    pl.smem = work > gather ? work : gather;
+    (void)dtype;
+    pl.chunk_len = kChunkLen;
+    pl.chunks = (vocab + pl.chunk_len - 1) / pl.chunk_len;
+    if (pl.chunks < 1) pl.chunks = 1;
+    if (pl.chunks > kMaxChunks) pl.chunks = 0;
+    pl.smem = static_cast<size_t>(kSW) * kWarpSmem;
+    // Unit length: a unit costs about its chunks plus kUnitOverhead chunks
+    // (its first chunk's full selection and its final list); units run in
+    // waves of one per warp. Take the length with the smallest makespan.
+    pl.unit_len = 1;
+    pl.units = pl.chunks;
+    if (pl.chunks > 0 && rows > 0) {
+        const long long warps = static_cast<long long>(sm_count()) * kSW;
+        constexpr int kUnitOverhead = 3;
+        long long best = -1;
+        for (int u = 1; u <= pl.chunks; ++u) {
+            const int per_row = (pl.chunks + u - 1) / u;
+            if (u > 1 && per_row == (pl.chunks + u - 2) / (u - 1)) continue;  // same split
+            const long long units = static_cast<long long>(rows) * per_row;
+            const long long waves = (units + warps - 1) / warps;
+            const long long cost = waves * (u + kUnitOverhead);
+            if (best < 0 || cost <= best) {
+                best = cost;
+                pl.unit_len = u;
+                pl.units = per_row;
+            }
+        }
+    }
     return pl;
 }
 
-cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s) {
-    const long long grid = static_cast<long long>(a.rows) * plan.slices;
-    if (grid <= 0) return cudaSuccess;
-    // Diagnostics (top-4 of sampled rows) use their own instantiation so the
-    // common path carries no top-4 state in its registers.
-    const bool top4 = a.out_top4 != nullptr && !a.top4_only;
-    void (*kern)(SampleArgs);
-    if (a.dtype == TQFS_DTYPE_F32) kern = top4 ? stream_kernel<0, true> : stream_kernel<0, false>;
-    else kern = top4 ? stream_kernel<1, true> : stream_kernel<1, false>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem));
-    kern<<<static_cast<unsigned>(grid), kThreads, plan.smem, s>>>(a);
+size_t stream_scratch(int rows, const Plan& pl, void* base, SampleArgs* a) {
+    const size_t ru = static_cast<size_t>(rows) * pl.units;
+    const size_t cand = align256(ru * kUnitCap * 8);
+    const size_t cn = align256(ru * 4);
+    const size_t th = align256(ru * 4);
+    const size_t t4 = align256(ru * 4 * 8);
+    const size_t wo = align256(static_cast<size_t>(rows) * pl.chunks * 2 * 4);
+    const size_t we = align256(static_cast<size_t>(rows) * kWinCap * 4);
+    if (base != nullptr && a != nullptr) {
+        unsigned char* b = static_cast<unsigned char*>(base);
+        a->cand = reinterpret_cast<unsigned long long*>(b);
+        b += cand;
+        a->cand_n = reinterpret_cast<int*>(b);
+        b += cn;
+        a->theta = reinterpret_cast<uint32_t*>(b);
+        b += th;
+        a->top4 = reinterpret_cast<unsigned long long*>(b);
+        b += t4;
+        a->win_off = reinterpret_cast<uint32_t*>(b);
+        b += wo;
+        a->win_ent = reinterpret_cast<uint32_t*>(b);
+    }
+    return cand + cn + th + t4 + wo + we;
+}
+
+cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t s) {
+    const long long total_units = static_cast<long long>(a_in.rows) * plan.units;
+    if (total_units <= 0) return cudaSuccess;
+    SampleArgs a = a_in;
+    a.chunks = plan.chunks;
+    a.chunk_len = plan.chunk_len;
+    a.unit_len = plan.unit_len;
+    a.units = plan.units;
+    cudaError_t e;
+    if (a.hist_off != nullptr && !a.top4_only) {
+        e = cudaFuncSetAttribute(window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kWindowSmem));
+        if (e != cudaSuccess) return e;
+        window_kernel<<<a.rows, kWinWarps * 32, kWindowSmem, s>>>(a);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    void (*kern)(SampleArgs, int) =
+        a.dtype == TQFS_DTYPE_F32 ? stream_kernel<0> : stream_kernel<1>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(plan.smem));
+    if (e != cudaSuccess) return e;
+    long long grid = sm_count();
+    const long long grid_needed = (total_units + kSW - 1) / kSW;
+    if (grid > grid_needed) grid = grid_needed;
+    const int top4_diag = a.out_top4 != nullptr && !a.top4_only;
+    kern<<<static_cast<unsigned>(grid), kST, plan.smem, s>>>(a, top4_diag);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t fsmem = static_cast<size_t>(kSurvCap) * 8;
+    e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(fsmem));
+    if (e != cudaSuccess) return e;
+    finalize_kernel<<<a.rows, kFT, fsmem, s>>>(a);
     return cudaGetLastError();
 }
 
