@@ -53,6 +53,7 @@ struct tqfs_handle {
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
     DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
+    DeviceBuffer tickets;      // per-row unit tickets, tagged with the call's number
     uint32_t epoch = 0;        // number of the last call
     size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
@@ -160,8 +161,14 @@ int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::Sampl
         if (e == cudaSuccess) e = cudaMemset(h->err_word.ptr, 0, 16);
         if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     }
+    if (h->tickets.bytes < static_cast<size_t>(rows) * 8) {  // new memory starts at zero
+        e = h->tickets.reserve(static_cast<size_t>(rows) * 8);
+        if (e == cudaSuccess) e = cudaMemset(h->tickets.ptr, 0, h->tickets.bytes);
+        if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
+    }
     if (++h->epoch == 0u) h->epoch = 1u;
     a.err_word = static_cast<uint32_t*>(h->err_word.ptr);
+    a.ticket = static_cast<unsigned long long*>(h->tickets.ptr);
     a.epoch = h->epoch;
     return TQFS_OK;
 }
@@ -287,6 +294,7 @@ int tqfs_destroy(tqfs_handle* h) {
     h->scratch.release();
     h->general.release();
     h->err_word.release();
+    h->tickets.release();
     h->h_logits.release();
     h->h_hist.release();
     h->h_off.release();

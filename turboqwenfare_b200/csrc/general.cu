@@ -93,9 +93,23 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
     float* E = g.e + static_cast<size_t>(blockIdx.x) * g.stride;
     unsigned long long* K = g.keys + static_cast<size_t>(blockIdx.x) * g.key_stride;
 
-    for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    // This CTA's general rows (rows blockIdx.x + gridDim.x * i), found by all
+    // threads at once and listed in shared memory.
+    __shared__ int list[kGenThreads];
+    __shared__ int nlist;
+    for (int r0 = blockIdx.x; r0 < a.rows; r0 += gridDim.x * kGenThreads) {
+    if (tid == 0) nlist = 0;
+    __syncthreads();
+    {
+        const int rr = r0 + gridDim.x * tid;
+        if (rr < a.rows && is_general(a, rr, a.params[rr])) list[atomicAdd(&nlist, 1)] = rr;
+    }
+    __syncthreads();
+    const int nl = nlist;
+#pragma unroll 1
+    for (int li = 0; li < nl; ++li) {
+        const int row = list[li];
         const tqfs_params p = a.params[row];
-        if (!is_general(a, row, p)) continue;
         const size_t base = static_cast<size_t>(row) * a.ld;
         // ---- penalised candidates in token order (mod.rs:90-99, 114-148) --
         for (int i = tid; i < V; i += kGenThreads) W[i] = logit_at<DT>(a.logits, base, i);
@@ -249,6 +263,8 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
             if (a.out_status != nullptr) a.out_status[row] = TQFS_ROW_OK;
         }
         __syncthreads();
+    }
+    __syncthreads();  // `list` is rewritten next round
     }
 }
 

@@ -37,6 +37,7 @@ struct SampleArgs {
     int chunk_len;             // ids per chunk
     int unit_len;              // chunks per unit (a warp's run of one row)
     int units;                 // units per row
+    unsigned long long* ticket;  // rows: (epoch << 32) | units of the row done
     uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
     uint32_t epoch;            // this call's number (never 0)
     int vec_ok;                // rows start on 16-byte boundaries

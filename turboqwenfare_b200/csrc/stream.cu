@@ -29,13 +29,14 @@
 //        bisection over the order values, keeping the count >= k; exact ties
 //        at the final value are resolved to the lowest ids.
 //
-// finalize_kernel: one CTA per row. Every chunk's theta is a lower bound of
-//   the row's k-th value, so the largest of them filters the candidate lists;
-//   the survivors are sorted, and softmax, top_p, min_p and the inverse-CDF
-//   draw run over the k survivors exactly as src/sampling/mod.rs:166-248 does
-//   (sequential f32 sums in order, by one thread).
+// Finalising: the warp that completes a row's last unit (per-row tickets)
+//   takes the union of the units' lists. Every unit's k-th value is a lower
+//   bound of the row's k-th value, so the largest of them filters the lists;
+//   the survivors' exact top-k is ranked, and softmax, top_p, min_p and the
+//   inverse-CDF draw run over it exactly as src/sampling/mod.rs:166-248 does
+//   (sequential f32 sums in order, by one lane).
 //
-// No kernel waits on another CTA or on a flag. The only waits are on a
+// No warp waits on another warp or CTA. The only waits are on a
 // warp's own bulk copies; each gives up after 2 s, sets the call's error word
 // and the rows report TQFS_ROW_ERR_TIMEOUT.
 #include <cuda_runtime.h>
@@ -55,12 +56,12 @@ constexpr int kSlots = 16;        // float4 register slots per lane per chunk
 constexpr int kChunkLen = kSlots * 32 * 4;  // 2,048 ids per chunk
 constexpr int kListCap = 384;     // keys of a warp's candidate list
 constexpr int kListOff = 16384;   // per-warp shared memory: chunk buffers (+ exchange),
-constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins
-constexpr int kWarpSmem = kBinsOff + 256 * 4;      // 20 KiB
+constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins,
+constexpr int kSortOff = kBinsOff + 256 * 4;       // ranked keys of a finalised row
+constexpr int kWarpSmem = kSortOff + kStreamMaxK * 8;  // 21 KiB
+constexpr int kCasTries = 1 << 20;                 // attempts at a row ticket
+constexpr int kMaxUnits = 32;                      // units per row (one lane each)
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
-constexpr int kFT = 256;          // threads per finalize CTA
-constexpr int kFW = kFT / 32;
-constexpr int kSurvCap = 8192;    // survivors the finaliser selects from in shared memory
 constexpr int kWinWarps = 8;      // warps of the window kernel
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
 
@@ -602,6 +603,204 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
     return c;
 }
 
+// Claims one of the row's units: tickets hold (epoch << 32) | units done, so
+// a word left by an earlier call (same row, other epoch) counts as zero.
+// True for the claim that completes the row. A word that cannot be updated
+// within kCasTries attempts marks the call as failed.
+__device__ __forceinline__ bool row_ticket(const SampleArgs& a, int row) {
+    unsigned long long* t = a.ticket + row;
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(t);
+    for (int i = 0; i < kCasTries; ++i) {
+        const unsigned long long nv = (old >> 32) == a.epoch
+                                          ? old + 1ull
+                                          : (static_cast<unsigned long long>(a.epoch) << 32) | 1ull;
+        const unsigned long long prev = atomicCAS(t, old, nv);
+        if (prev == old) return static_cast<int>(nv & 0xFFFFFFFFull) == a.units;
+        old = prev;
+    }
+    atomicMax(a.err_word, a.epoch);
+    return false;
+}
+
+// Ranks the n distinct keys src[0..n) descending into dst (warp).
+__device__ __forceinline__ void warp_rank_sort(const unsigned long long* src, int n,
+                                               unsigned long long* dst) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < n; i += 32) {
+        const unsigned long long key = src[i];
+        int r = 0;
+        for (int j = 0; j < n; ++j) r += src[j] > key;
+        dst[r] = key;
+    }
+    __syncwarp();
+}
+
+// Finalises a row in one warp once all its units have written their lists:
+// greedy rows take the top-4 (src/runtime/decode.rs:48-64); sampled rows the
+// exact top-k by (value desc, id asc) of the union of the units' lists (every
+// row top-k member is in its unit's top-k), then softmax, top_p, min_p and
+// the inverse-CDF draw as src/sampling/mod.rs:166-248 does, the sequential
+// f32 sums in order by one lane. L (kListCap keys) and S (128 keys) are the
+// warp's shared memory.
+__device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool greedy, int k,
+                                          unsigned long long* L, unsigned long long* S,
+                                          unsigned int* bins, int* counter) {
+    const int lane = threadIdx.x & 31;
+    __threadfence();  // the other units' lists are visible after their tickets
+    const int U = a.units;
+    const size_t base = static_cast<size_t>(row) * U;
+    // Loads issued together: the lists' lengths and bounds, the row's knobs.
+    const int m_raw = (!greedy && lane < U) ? __ldcg(a.cand_n + base + lane) : 0;
+    const uint32_t th_u = (!greedy && lane < U) ? __ldcg(a.theta + base + lane) : 0u;
+    const tqfs_params p = greedy ? tqfs_params{} : a.params[row];
+    int token = 0;
+    const bool timed_out = *reinterpret_cast<volatile uint32_t*>(a.err_word) == a.epoch;
+    if (timed_out) {  // the units' lists may be missing: report and stop
+        if (lane == 0) {
+            if (a.out_token != nullptr) a.out_token[row] = -1;
+            if (a.out_status != nullptr) a.out_status[row] = TQFS_ROW_ERR_TIMEOUT;
+        }
+        __syncwarp();
+        return;
+    }
+    if (greedy || a.out_top4 != nullptr) {
+        unsigned long long t[4] = {0ull, 0ull, 0ull, 0ull};
+        for (int i = lane; i < U * 4; i += 32) top4_insert(t, __ldcg(a.top4 + base * 4 + i));
+        unsigned long long o[4];
+        warp_top4(t, o, lane);
+        if (lane == 0 && a.out_top4 != nullptr) {
+            for (int r = 0; r < 4; ++r) {
+                tqfs_candidate cnd;
+                cnd.token = o[r] ? key_token(o[r]) : 0u;
+                cnd.logit = o[r] ? key_value(o[r]) : -INFINITY;
+                a.out_top4[static_cast<size_t>(row) * 4 + r] = cnd;
+            }
+        }
+        token = o[0] ? static_cast<int>(key_token(o[0])) : 0;
+    }
+    if (!greedy) {
+        // Lists: lane u holds unit u's length and bound (units <= 32); the
+        // list offsets go to S until the survivors are ranked there.
+        const int m_u = min(max(m_raw, 0), kUnitCap);
+        uint32_t tb = th_u;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tb = max(tb, __shfl_xor_sync(0xFFFFFFFFu, tb, o));
+        const unsigned long long kb = static_cast<unsigned long long>(tb) << 32;
+        const int off_u = warp_excl_scan(m_u, lane);
+        const int total = __shfl_sync(0xFFFFFFFFu, off_u + m_u, 31);
+        int* offs = reinterpret_cast<int*>(S);
+        if (lane < U) offs[lane] = off_u;
+        __syncwarp();
+        // Gather the keys at or above the row bound (every row top-k member
+        // is one), keeping L short with exact top-k cuts.
+        int n = 0;
+        for (int q0 = 0; q0 < total; q0 += 32) {
+            const int q = q0 + lane;
+            unsigned long long key = 0ull;
+            bool keep = false;
+            if (q < total) {
+                int lo = 0, hi = U;  // the unit u with offs[u] <= q < offs[u + 1]
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (offs[mid] <= q) lo = mid; else hi = mid;
+                }
+                key = __ldcg(a.cand + (base + lo) * kUnitCap + (q - offs[lo]));
+                keep = key >= kb;
+            }
+            const unsigned ball = __ballot_sync(0xFFFFFFFFu, keep);
+            if (n + 32 > kListCap) warp_keep_top(L, &n, k, bins);
+            if (keep) L[n + __popc(ball & ((1u << lane) - 1u))] = key;
+            n += __popc(ball);
+            __syncwarp();
+        }
+        warp_keep_top(L, &n, k, bins);
+        const int kk = n;  // min(k, survivors)
+        warp_rank_sort(L, kk, S);
+        // softmax over the survivors (src/sampling/mod.rs:166-190)
+        float* E = reinterpret_cast<float*>(L);                        // kk floats
+        unsigned long long* PK = L + kStreamMaxK / 2;                 // kk keys
+        float* P = reinterpret_cast<float*>(L + kStreamMaxK / 2 + kStreamMaxK);  // kk floats
+        const float first = kk > 0 ? key_value(S[0]) : 0.0f;
+        const float mx = (kk > 0 && first == first) ? first : -INFINITY;
+        for (int i = lane; i < kk; i += 32)
+            E[i] = exp_f32(__fdiv_rn(__fsub_rn(key_value(S[i]), mx), p.temperature));
+        __syncwarp();
+        float total_e = -0.0f;
+        if (lane == 0)
+            for (int i = 0; i < kk; ++i) total_e = __fadd_rn(total_e, E[i]);
+        total_e = __shfl_sync(0xFFFFFFFFu, total_e, 0);
+        for (int i = lane; i < kk; i += 32) {
+            const float pv = total_e > 0.0f ? __fdiv_rn(E[i], total_e) : E[i];
+            PK[i] = make_key(order32(pv), key_token(S[i]));
+        }
+        __syncwarp();
+        warp_rank_sort(PK, kk, S);  // probability keys in draw order
+        for (int i = lane; i < kk; i += 32) P[i] = key_value(S[i]);
+        __syncwarp();
+        // top_p, min_p, draw (src/sampling/mod.rs:195-248)
+        int keep = kk;
+        if (lane == 0) {
+            if (!(p.top_p >= 1.0f)) {
+                float cum = 0.0f;
+                int c = 0;
+                for (int i = 0; i < kk; ++i) {
+                    cum = __fadd_rn(cum, P[i]);
+                    ++c;
+                    if (cum >= p.top_p) break;
+                }
+                keep = c < 1 ? 1 : c;
+                if (keep > kk) keep = kk;
+            }
+            if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
+                const float floor = __fmul_rn(p.min_p, P[0]);
+                int c = 0;
+                while (c < keep && P[c] >= floor) ++c;
+                keep = c < 1 ? 1 : c;
+            }
+            int tok = 0;
+            if (keep > 0) {
+                int pick = 0;
+                float total2 = -0.0f;
+                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, P[i]);
+                if (isfinite(total2) && total2 > 0.0f) {
+                    float u;
+                    if (a.uniforms != nullptr) {
+                        u = a.uniforms[row];
+                    } else {
+                        uint64_t st[4];
+                        uint64_t* sp = a.rng_state + static_cast<size_t>(row) * 4;
+                        for (int q = 0; q < 4; ++q) st[q] = sp[q];
+                        u = xoshiro_next_f32(st);
+                        for (int q = 0; q < 4; ++q) sp[q] = st[q];
+                    }
+                    const float target = __fmul_rn(u, total2);
+                    float cum = 0.0f;
+                    pick = keep - 1;
+                    for (int i = 0; i < keep; ++i) {
+                        cum = __fadd_rn(cum, P[i]);
+                        if (cum >= target) {
+                            pick = i;
+                            break;
+                        }
+                    }
+                }
+                tok = static_cast<int>(key_token(S[pick]));
+            }
+            token = tok;
+        }
+        token = __shfl_sync(0xFFFFFFFFu, token, 0);
+        keep = __shfl_sync(0xFFFFFFFFu, keep, 0);
+        if (a.out_probs != nullptr)
+            for (int i = lane; i < keep; i += 32)
+                a.out_probs[static_cast<size_t>(row) * a.ld + key_token(S[i])] = P[i];
+    }
+    if (lane == 0) {
+        if (a.out_token != nullptr) a.out_token[row] = token;
+        if (a.out_status != nullptr) a.out_status[row] = TQFS_ROW_OK;
+    }
+    __syncwarp();
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_diag) {
     constexpr int ES = Raw<DT>::kES;
@@ -616,6 +815,7 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
     float* xch = reinterpret_cast<float*>(wbase + 2 * Raw<DT>::kBuf);
     unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase + kListOff);
     unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + kBinsOff);
+    unsigned long long* S = reinterpret_cast<unsigned long long*>(wbase + kSortOff);
     if (lane == 0) {
         mbar_init(&wbar[warp][0], 1);
         mbar_init(&wbar[warp][1], 1);
@@ -623,6 +823,9 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
     }
     __syncwarp();
 
+    // Launched right behind the window kernel: wait for its buckets (a no-op
+    // when there is no window kernel in front).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int nw = static_cast<int>(gridDim.x) * kSW;
     const int nw_row = nw % a.rows, nw_u = nw / a.rows;
     const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
@@ -698,6 +901,7 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
     bool sel = false;
     uint32_t th_ord = 0u;
     Top4 t4;
+    bool failed = false;
 
 #pragma unroll 1
     while (cur.mode != -1) {
@@ -706,23 +910,23 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
         w2 = info_word(a, p2, same_unit(p2, nn), lane);
         uint32_t enn[4];
         load_entries(nxt, enn);
-        {
+        if (!failed) {
             const bool ok = mbar_wait_bounded(&wbar[warp][b], (parity >> b) & 1u, kWaitBudgetNs);
             parity ^= 1u << b;
             if (!__all_sync(0xFFFFFFFFu, ok)) {
                 // A copy did not land in time: report it, wait (bounded) for
-                // the other buffer's copy so none lands after exit, and stop.
+                // the other buffer's copy, and from here on only count this
+                // warp's units so their rows still report.
+                failed = true;
                 if (lane == 0) {
                     atomicMax(a.err_word, a.epoch);
                     mbar_wait_bounded(&wbar[warp][b ^ 1], (parity >> (b ^ 1)) & 1u, kWaitBudgetNs);
                 }
-                __syncwarp();
-                return;
             }
         }
         __syncwarp();
 
-        if (cur.mode == kModeGreedy || cur.mode == kModeStream) {
+        if (!failed && (cur.mode == kModeGreedy || cur.mode == kModeStream)) {
             const int base_id = cur.chunk * kChunkLen;
             const int n_here = chunk_len(cur);
             const size_t uslot = static_cast<size_t>(cur.row) * a.units + cur.u;
@@ -831,9 +1035,18 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
                 }
             }
         }
+        // ---- 7. the last unit of a row to finish finalises the row -------
+        if (cur.last && (cur.mode == kModeGreedy || cur.mode == kModeStream)) {
+            __threadfence();  // this unit's lists before its ticket
+            __syncwarp();
+            bool last = false;
+            if (lane == 0) last = row_ticket(a, cur.row);
+            if (__shfl_sync(0xFFFFFFFFu, last, 0))
+                finalize_row(a, cur.row, cur.mode == kModeGreedy, cur.k, L, S, bins, &wcount[warp]);
+        }
         // Every value of the buffer has been read: refill it.
         __syncwarp();
-        start_copy(nn, b);
+        if (!failed) start_copy(nn, b);
 
         // ---- rotate -------------------------------------------------------
 #pragma unroll
@@ -856,6 +1069,9 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
     uint32_t* tbl = start + kMaxChunks + 1;               // kWinWarps x kChunkLen/2
     uint16_t* buf = reinterpret_cast<uint16_t*>(tbl + kWinWarps * (kChunkLen / 2));  // kWinCap
     __shared__ uint32_t nd[kWinWarps];
+    // The stream kernel may launch now; it waits for this grid to finish
+    // (griddepcontrol.wait) before it reads the buckets.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NT = kWinWarps * 32;
@@ -941,323 +1157,6 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
     }
 }
 
-struct FinalShared {
-    unsigned long long topk[kStreamMaxK];  // top-k keys, then probability keys
-    unsigned long long pkey[kStreamMaxK];
-    float e[kStreamMaxK];
-    float prob[kStreamMaxK];               // probabilities in draw order
-    unsigned long long w4[kFW][4];
-    unsigned long long top4[4];
-    int noff[kMaxChunks + 1];              // prefix of the units' list lengths
-    uint32_t wmax[kFW];
-    unsigned int hist[256];                // radix-select digit counts
-    unsigned long long wcnt;
-    int n;
-    int rdig, rabove;
-    float total;
-    int result[2];
-};
-
-// One CTA per row: merges the units' lists written by stream_kernel and
-// finalises the row (greedy: top-4; sampled: exact top-k, softmax, top_p,
-// min_p, draw as src/sampling/mod.rs:166-248).
-__global__ void __launch_bounds__(kFT) finalize_kernel(SampleArgs a) {
-    extern __shared__ __align__(16) unsigned char fdyn[];
-    __shared__ FinalShared fs;
-    unsigned long long* g = reinterpret_cast<unsigned long long*>(fdyn);  // kSurvCap keys
-    const int row = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const tqfs_params p = a.top4_only ? tqfs_params{} : a.params[row];
-    long long hs = 0, he = 0;
-    if (a.hist_off != nullptr && !a.top4_only) {
-        hs = a.hist_off[row];
-        he = a.hist_off[row + 1];
-    }
-    long long ws, wl;
-    const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab, a.top4_only != 0, &ws, &wl);
-    if (mode == kModeGeneral) return;  // the general kernel's row
-    const bool greedy = mode == kModeGreedy;
-    const int C = a.units;
-    const size_t base = static_cast<size_t>(row) * C;
-    int token = 0;
-
-    if (greedy || a.out_top4 != nullptr) {
-        unsigned long long t[4] = {0ull, 0ull, 0ull, 0ull};
-        for (int i = tid; i < C * 4; i += kFT) top4_insert(t, __ldcg(a.top4 + base * 4 + i));
-        unsigned long long o[4];
-        warp_top4(t, o, lane);
-        if (lane == 0)
-            for (int r = 0; r < 4; ++r) fs.w4[warp][r] = o[r];
-        __syncthreads();
-        if (tid == 0) {
-            unsigned long long m[4] = {0ull, 0ull, 0ull, 0ull};
-            for (int w = 0; w < kFW; ++w)
-                for (int r = 0; r < 4; ++r) top4_insert(m, fs.w4[w][r]);
-            for (int r = 0; r < 4; ++r) fs.top4[r] = m[r];
-            if (a.out_top4 != nullptr) {
-                for (int r = 0; r < 4; ++r) {
-                    tqfs_candidate cnd;
-                    cnd.token = m[r] ? key_token(m[r]) : 0u;
-                    cnd.logit = m[r] ? key_value(m[r]) : -INFINITY;
-                    a.out_top4[static_cast<size_t>(row) * 4 + r] = cnd;
-                }
-            }
-        }
-        __syncthreads();
-        token = fs.top4[0] ? static_cast<int>(key_token(fs.top4[0])) : 0;
-    }
-
-    if (!greedy) {
-        const int k = static_cast<int>(p.top_k);
-        // ---- list lengths (prefix) and the row bound -----------------------
-        uint32_t tb = 0u;
-        for (int c = tid; c < C; c += kFT) {
-            fs.noff[c + 1] = __ldcg(a.cand_n + base + c);
-            tb = max(tb, __ldcg(a.theta + base + c));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tb = max(tb, __shfl_xor_sync(0xFFFFFFFFu, tb, o));
-        if (lane == 0) fs.wmax[warp] = tb;
-        if (tid == 0) {
-            fs.noff[0] = 0;
-            fs.n = 0;
-        }
-        __syncthreads();
-        if (warp == 0) {
-            const int per = (C + 31) / 32;
-            const int b0 = lane * per;
-            int s = 0;
-            for (int i = 0; i < per; ++i)
-                if (b0 + i < C) s += fs.noff[b0 + i + 1];
-            int run = warp_excl_scan(s, lane);
-            for (int i = 0; i < per; ++i) {
-                if (b0 + i < C) {
-                    run += fs.noff[b0 + i + 1];
-                    fs.noff[b0 + i + 1] = run;
-                }
-            }
-        }
-        tb = 0u;
-        for (int w = 0; w < kFW; ++w) tb = max(tb, fs.wmax[w]);
-        __syncthreads();
-        const unsigned long long kb = static_cast<unsigned long long>(tb) << 32;
-        const int total_n = fs.noff[C];
-        // ---- gather the survivors: entry q of the concatenated lists -------
-        for (int q0 = 0; q0 < total_n; q0 += kFT * 4) {
-            unsigned long long key[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int q = q0 + u * kFT + tid;
-                key[u] = 0ull;
-                if (q < total_n) {
-                    int lo = 0, hi = C;  // the chunk c with noff[c] <= q < noff[c+1]
-                    while (hi - lo > 1) {
-                        const int mid = (lo + hi) >> 1;
-                        if (fs.noff[mid] <= q) lo = mid; else hi = mid;
-                    }
-                    key[u] = __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo]));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (q0 + u * kFT + tid < total_n && key[u] >= kb) {
-                    const int idx = atomicAdd(&fs.n, 1);
-                    if (idx < kSurvCap) g[idx] = key[u];
-                }
-            }
-        }
-        __syncthreads();
-        int m = fs.n;
-        if (m > kSurvCap) {
-            // Rare (heavy ties): the exact k-th key by bisection over the
-            // lists, then exactly the k keys at or above it.
-            unsigned long long kth = 0ull;
-            for (int bit = 63; bit >= 0; --bit) {
-                const unsigned long long cand = kth | (1ull << bit);
-                unsigned long long cnt = 0ull;
-                for (int q = tid; q < total_n; q += kFT) {
-                    int lo = 0, hi = C;
-                    while (hi - lo > 1) {
-                        const int mid = (lo + hi) >> 1;
-                        if (fs.noff[mid] <= q) lo = mid; else hi = mid;
-                    }
-                    cnt += __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo])) >= cand;
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
-                if (tid == 0) fs.wcnt = 0ull;
-                __syncthreads();
-                if (lane == 0) atomicAdd(&fs.wcnt, cnt);
-                __syncthreads();
-                if (fs.wcnt >= static_cast<unsigned long long>(k)) kth = cand;
-                __syncthreads();
-            }
-            if (tid == 0) fs.n = 0;
-            __syncthreads();
-            for (int q = tid; q < total_n; q += kFT) {
-                int lo = 0, hi = C;
-                while (hi - lo > 1) {
-                    const int mid = (lo + hi) >> 1;
-                    if (fs.noff[mid] <= q) lo = mid; else hi = mid;
-                }
-                const unsigned long long key =
-                    __ldcg(a.cand + (base + lo) * kUnitCap + (q - fs.noff[lo]));
-                if (key >= kth) g[atomicAdd(&fs.n, 1)] = key;
-            }
-            __syncthreads();
-            m = fs.n;
-        }
-        // ---- the k-th largest survivor key (radix select, 8-bit digits) ----
-        unsigned long long kth = 0ull;
-        if (m > k) {
-            int remaining = k;
-            for (int shift = 56; shift >= 0; shift -= 8) {
-                for (int i = tid; i < 256; i += kFT) fs.hist[i] = 0u;
-                __syncthreads();
-                const unsigned long long hmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
-                for (int i = tid; i < m; i += kFT) {
-                    const unsigned long long key = g[i];
-                    if ((key & hmask) == kth)
-                        atomicAdd(&fs.hist[static_cast<int>((key >> shift) & 255u)], 1u);
-                }
-                __syncthreads();
-                if (warp == 0) {
-                    // lane l covers digits 255 - 8l down to 248 - 8l
-                    int sum = 0;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) sum += static_cast<int>(fs.hist[255 - 8 * lane - i]);
-                    const int above = warp_excl_scan(sum, lane);
-                    if (above < remaining && remaining <= above + sum) {
-                        int c = above;
-                        for (int i = 0; i < 8; ++i) {
-                            const int d = 255 - 8 * lane - i;
-                            const int h = static_cast<int>(fs.hist[d]);
-                            if (c + h >= remaining) {
-                                fs.rdig = d;
-                                fs.rabove = c;
-                                break;
-                            }
-                            c += h;
-                        }
-                    }
-                }
-                __syncthreads();
-                kth |= static_cast<unsigned long long>(fs.rdig) << shift;
-                remaining -= fs.rabove;
-                __syncthreads();
-            }
-        }
-        // ---- the top-k keys, ranked by (value desc, id asc) -----------------
-        const int kk = min(k, m);
-        if (tid == 0) fs.n = 0;
-        __syncthreads();
-        for (int i = tid; i < m; i += kFT) {
-            const unsigned long long key = g[i];
-            if (key >= kth) fs.pkey[atomicAdd(&fs.n, 1)] = key;
-        }
-        __syncthreads();
-        if (tid < kk) {
-            const unsigned long long key = fs.pkey[tid];
-            int r = 0;
-            for (int q = 0; q < kk; ++q) r += fs.pkey[q] > key;
-            fs.topk[r] = key;
-        }
-        __syncthreads();
-        // softmax over the survivors (src/sampling/mod.rs:166-190)
-        const float first = kk > 0 ? key_value(fs.topk[0]) : 0.0f;
-        const float mx = (kk > 0 && first == first) ? first : -INFINITY;
-        if (tid < kk) {
-            const float v = key_value(fs.topk[tid]);
-            fs.e[tid] = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float total = -0.0f;
-            for (int i = 0; i < kk; ++i) total = __fadd_rn(total, fs.e[i]);
-            fs.total = total;
-        }
-        __syncthreads();
-        const float total = fs.total;
-        float pv = 0.0f;
-        unsigned long long pk = 0ull;
-        if (tid < kk) {
-            pv = total > 0.0f ? __fdiv_rn(fs.e[tid], total) : fs.e[tid];
-            pk = make_key(order32(pv), key_token(fs.topk[tid]));
-            fs.pkey[tid] = pk;
-        }
-        __syncthreads();
-        if (tid < kk) {
-            int r = 0;
-            for (int q = 0; q < kk; ++q) r += fs.pkey[q] > pk;
-            fs.topk[r] = pk;  // probability keys in draw order
-            fs.prob[r] = pv;
-        }
-        __syncthreads();
-        // top_p, min_p, draw (src/sampling/mod.rs:195-248)
-        if (tid == 0) {
-            int keep = kk;
-            if (!(p.top_p >= 1.0f)) {
-                float cum = 0.0f;
-                int n = 0;
-                for (int i = 0; i < kk; ++i) {
-                    cum = __fadd_rn(cum, fs.prob[i]);
-                    ++n;
-                    if (cum >= p.top_p) break;
-                }
-                keep = n < 1 ? 1 : n;
-                if (keep > kk) keep = kk;
-            }
-            if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
-                const float floor = __fmul_rn(p.min_p, fs.prob[0]);
-                int n = 0;
-                while (n < keep && fs.prob[n] >= floor) ++n;
-                keep = n < 1 ? 1 : n;
-            }
-            int tok = 0;
-            if (keep > 0) {
-                int pick = 0;
-                float total2 = -0.0f;
-                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, fs.prob[i]);
-                if (isfinite(total2) && total2 > 0.0f) {
-                    float u;
-                    if (a.uniforms != nullptr) {
-                        u = a.uniforms[row];
-                    } else {
-                        uint64_t st[4];
-                        uint64_t* sp = a.rng_state + static_cast<size_t>(row) * 4;
-                        for (int q = 0; q < 4; ++q) st[q] = sp[q];
-                        u = xoshiro_next_f32(st);
-                        for (int q = 0; q < 4; ++q) sp[q] = st[q];
-                    }
-                    const float target = __fmul_rn(u, total2);
-                    float cum = 0.0f;
-                    pick = keep - 1;
-                    for (int i = 0; i < keep; ++i) {
-                        cum = __fadd_rn(cum, fs.prob[i]);
-                        if (cum >= target) {
-                            pick = i;
-                            break;
-                        }
-                    }
-                }
-                tok = static_cast<int>(key_token(fs.topk[pick]));
-            }
-            fs.result[0] = tok;
-            fs.result[1] = keep;
-        }
-        __syncthreads();
-        token = fs.result[0];
-        const int keep = fs.result[1];
-        if (a.out_probs != nullptr && tid < keep)
-            a.out_probs[static_cast<size_t>(row) * a.ld + key_token(fs.topk[tid])] = fs.prob[tid];
-    }
-    if (tid == 0) {
-        const bool timed_out = a.err_word != nullptr && *a.err_word == a.epoch;
-        if (a.out_token != nullptr) a.out_token[row] = timed_out ? -1 : token;
-        if (a.out_status != nullptr) a.out_status[row] = timed_out ? TQFS_ROW_ERR_TIMEOUT : TQFS_ROW_OK;
-    }
-}
-
 __global__ void fill_empty_kernel(int rows, int32_t* out_token, int32_t* out_status,
                                   tqfs_candidate* out_top4) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1300,15 +1199,16 @@ Plan plan_stream(int rows, int vocab, int dtype) {
     // Unit length: a unit costs about its chunks plus kUnitOverhead chunks
     // (its first chunk's full selection and its final list); units run in
     // waves of one per warp. Take the length with the smallest makespan.
-    pl.unit_len = 1;
-    pl.units = pl.chunks;
+    pl.unit_len = (pl.chunks + kMaxUnits - 1) / kMaxUnits;
+    pl.units = pl.chunks > 0 ? (pl.chunks + pl.unit_len - 1) / pl.unit_len : 0;
     if (pl.chunks > 0 && rows > 0) {
         const long long warps = static_cast<long long>(sm_count()) * kSW;
         constexpr int kUnitOverhead = 3;
         long long best = -1;
-        for (int u = 1; u <= pl.chunks; ++u) {
+        const int u_min = (pl.chunks + kMaxUnits - 1) / kMaxUnits;
+        for (int u = u_min; u <= pl.chunks; ++u) {
             const int per_row = (pl.chunks + u - 1) / u;
-            if (u > 1 && per_row == (pl.chunks + u - 2) / (u - 1)) continue;  // same split
+            if (u > u_min && per_row == (pl.chunks + u - 2) / (u - 1)) continue;  // same split
             const long long units = static_cast<long long>(rows) * per_row;
             const long long waves = (units + warps - 1) / warps;
             const long long cost = waves * (u + kUnitOverhead);
@@ -1356,7 +1256,8 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     a.unit_len = plan.unit_len;
     a.units = plan.units;
     cudaError_t e;
-    if (a.hist_off != nullptr && !a.top4_only) {
+    const bool window = a.hist_off != nullptr && !a.top4_only;
+    if (window) {
         e = cudaFuncSetAttribute(window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kWindowSmem));
         if (e != cudaSuccess) return e;
@@ -1373,15 +1274,17 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     const long long grid_needed = (total_units + kSW - 1) / kSW;
     if (grid > grid_needed) grid = grid_needed;
     const int top4_diag = a.out_top4 != nullptr && !a.top4_only;
-    kern<<<static_cast<unsigned>(grid), kST, plan.smem, s>>>(a, top4_diag);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    const size_t fsmem = static_cast<size_t>(kSurvCap) * 8;
-    e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(fsmem));
-    if (e != cudaSuccess) return e;
-    finalize_kernel<<<a.rows, kFT, fsmem, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kST);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = window ? 1 : 0;  // overlap its launch with the window kernel
+    return cudaLaunchKernelEx(&cfg, kern, a, top4_diag);
 }
 
 cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,
