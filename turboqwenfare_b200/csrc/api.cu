@@ -189,8 +189,15 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
     cudaError_t e;
     {
-        TimingScope ts(h, s, 0);
-        e = tqfs::launch_stream(a, plan, s);
+        const bool window = a.hist_off != nullptr && !a.top4_only;
+        {
+            TimingScope ts(h, s, 2);
+            e = tqfs::launch_window(a, plan, s);
+        }
+        if (e == cudaSuccess) {
+            TimingScope ts(h, s, 0);
+            e = tqfs::launch_stream(a, plan, s, window && !h->timing);
+        }
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
     if (a.top4_only) return TQFS_OK;

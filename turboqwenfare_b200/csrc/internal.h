@@ -68,7 +68,10 @@ Plan plan_stream(int rows, int vocab, int dtype);
 // Bytes of stream-path scratch for `rows`; with a non-null base, also points
 // a's scratch fields into [base, base + bytes).
 size_t stream_scratch(int rows, const Plan& plan, void* base, SampleArgs* a);
-cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s);
+// The window pre-pass (a no-op without a history), then the stream kernel;
+// after_window lets the stream kernel's launch overlap the pre-pass.
+cudaError_t launch_window(const SampleArgs& a, const Plan& plan, cudaStream_t s);
+cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool after_window);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
 cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s);
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,

@@ -132,5 +132,7 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
 
     mark_unhandled_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token_dev, out_status_dev);
     if (cudaGetLastError() != cudaSuccess) return TQFS_ERR_CUDA;
-    return launch_stream(a, plan, s) == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
+    if (launch_window(a, plan, s) != cudaSuccess) return TQFS_ERR_CUDA;
+    const bool window = hist_off_dev != nullptr;
+    return launch_stream(a, plan, s, window) == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
 }

@@ -1247,32 +1247,40 @@ size_t stream_scratch(int rows, const Plan& pl, void* base, SampleArgs* a) {
     return cand + cn + th + t4 + wo + we;
 }
 
-cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t s) {
-    const long long total_units = static_cast<long long>(a_in.rows) * plan.units;
-    if (total_units <= 0) return cudaSuccess;
+namespace {
+SampleArgs with_plan(const SampleArgs& a_in, const Plan& plan) {
     SampleArgs a = a_in;
     a.chunks = plan.chunks;
     a.chunk_len = plan.chunk_len;
     a.unit_len = plan.unit_len;
     a.units = plan.units;
-    cudaError_t e;
-    const bool window = a.hist_off != nullptr && !a.top4_only;
-    if (window) {
-        e = cudaFuncSetAttribute(window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kWindowSmem));
-        if (e != cudaSuccess) return e;
-        window_kernel<<<a.rows, kWinWarps * 32, kWindowSmem, s>>>(a);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-    }
+    return a;
+}
+}  // namespace
+
+cudaError_t launch_window(const SampleArgs& a_in, const Plan& plan, cudaStream_t s) {
+    if (a_in.rows <= 0 || plan.units <= 0 || a_in.hist_off == nullptr || a_in.top4_only) return cudaSuccess;
+    const SampleArgs a = with_plan(a_in, plan);
+    cudaError_t e = cudaFuncSetAttribute(window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kWindowSmem));
+    if (e != cudaSuccess) return e;
+    window_kernel<<<a.rows, kWinWarps * 32, kWindowSmem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t s, bool after_window) {
+    const long long total_units = static_cast<long long>(a_in.rows) * plan.units;
+    if (total_units <= 0) return cudaSuccess;
+    const SampleArgs a = with_plan(a_in, plan);
     void (*kern)(SampleArgs, int) =
         a.dtype == TQFS_DTYPE_F32 ? stream_kernel<0> : stream_kernel<1>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(plan.smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(plan.smem));
     if (e != cudaSuccess) return e;
+    // Every SM gets a CTA (warps are numbered across CTAs first, so the units
+    // spread over all SMs even when there are fewer units than warps).
     long long grid = sm_count();
-    const long long grid_needed = (total_units + kSW - 1) / kSW;
-    if (grid > grid_needed) grid = grid_needed;
+    if (grid > total_units) grid = total_units;
     const int top4_diag = a.out_top4 != nullptr && !a.top4_only;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -1283,7 +1291,7 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = window ? 1 : 0;  // overlap its launch with the window kernel
+    cfg.numAttrs = after_window ? 1 : 0;  // overlap its launch with the window kernel
     return cudaLaunchKernelEx(&cfg, kern, a, top4_diag);
 }
 
