@@ -187,6 +187,39 @@ int tqfs_apply_penalties(tqfs_handle* handle, const void* logits_dev, int dtype,
                          float* out_dev, void* stream);
 
 /*
+ * MTP draft verification for `seqs` sequences of `draft_len` drafts.
+ * Replaces `verify_pair` (src/runtime/mtp.rs:92-104) for a batch and extends
+ * it to sampled rows:
+ *   target_dev: seqs x (draft_len + 1) rows (row s*(L+1)+j scores position j;
+ *               row s*(L+1)+L is the bonus position); draft_dev: seqs x L rows;
+ *               both with row stride ld, dtype F32 or BF16;
+ *   drafts_dev: seqs x L int32 draft tokens; params_dev: one tqfs_params per
+ *               sequence (penalties must be neutral); uniforms_dev: seqs x
+ *               (L + 1) floats on the 2^-24 grid, u_j for position j and u_L
+ *               for the replacement or bonus token.
+ * temperature 0: position j accepts iff the target row's argmax (the first
+ * entry of top_logit_candidates) equals the draft, as verify_pair does.
+ * Otherwise, with q the sampler's post-filter distribution (kept probability /
+ * draw total; a point mass when that total is not a positive number): accept
+ * iff u_j * q_draft(x) < q_target(x) in f32. At the first rejection the token
+ * is drawn from the residual max(0, q_target - q_draft) (each id rounded to a
+ * multiple of 2^-62, summed exactly; the first id, ascending, whose prefix
+ * exceeds floor(floor(u_L * 2^32) * total / 2^32)); with no residual mass,
+ * from the target row with u_L. All drafts accepted: the bonus token is the
+ * sampler's draw from row L with u_L (its argmax at temperature 0).
+ * Outputs per sequence: out_accepted (drafts accepted, 0..L), out_token (the
+ * token to append), out_status (optional; TQFS_ROW_ERR_UNSUPPORTED with
+ * -1/-1 when a penalty is active); out_mask_dev (optional) gets the decision
+ * of every position. No counterpart in the reference for sampled rows (it
+ * verifies greedily only).
+ */
+int tqfs_mtp_verify(tqfs_handle* handle, const void* target_dev, const void* draft_dev, int dtype,
+                    int seqs, int draft_len, int vocab, int64_t ld, const int32_t* drafts_dev,
+                    const tqfs_params* params_dev, const float* uniforms_dev,
+                    int32_t* out_accepted_dev, int32_t* out_token_dev, uint8_t* out_mask_dev,
+                    int32_t* out_status_dev, void* stream);
+
+/*
  * tqfs_sample without any GPU allocation. No counterpart in the reference
  * (its sampler is host code); it exists for callers that cannot call
  * cudaMalloc: hosts whose GPU memory is already reserved by their own pool,

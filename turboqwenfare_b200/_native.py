@@ -38,7 +38,7 @@ EXPORTS = [
     "tqfs_version", "tqfs_status_string", "tqfs_create", "tqfs_destroy", "tqfs_last_error",
     "tqfs_set_timing", "tqfs_get_timing", "tqfs_xoshiro_from_seed", "tqfs_xoshiro_next_u64",
     "tqfs_xoshiro_next_f32", "tqfs_sample", "tqfs_sample_host", "tqfs_top_logit_candidates",
-    "tqfs_apply_penalties", "tqfs_sample_static", "tqfs_sampler_new", "tqfs_sampler_is_greedy", "tqfs_sampler_select", "tqfs_sampler_get_state",
+    "tqfs_apply_penalties", "tqfs_mtp_verify", "tqfs_sample_static", "tqfs_sampler_new", "tqfs_sampler_is_greedy", "tqfs_sampler_select", "tqfs_sampler_get_state",
     "tqfs_sampler_free",
 ]
 
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
     L.tqfs_top_logit_candidates.argtypes = [vp, vp, i32, i32, i32, i64, vp, vp]
     L.tqfs_apply_penalties.argtypes = [vp, vp, i32, i32, i32, i64, vp, vp, vp, vp, vp]
     L.tqfs_sample_static.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp]
+    L.tqfs_mtp_verify.argtypes = [vp, vp, vp, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp]
     L.tqfs_sampler_new.argtypes = [vp, ctypes.POINTER(Params), i32, u64, ctypes.POINTER(vp)]
     L.tqfs_sampler_is_greedy.argtypes = [vp]
     L.tqfs_sampler_select.argtypes = [vp, vp, i64, vp, i64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32)]

@@ -54,6 +54,7 @@ struct tqfs_handle {
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
     DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
     DeviceBuffer tickets;      // per-row unit tickets, tagged with the call's number
+    DeviceBuffer mtp;          // MTP verify workspaces
     uint32_t epoch = 0;        // number of the last call
     size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
@@ -302,6 +303,7 @@ int tqfs_destroy(tqfs_handle* h) {
     h->general.release();
     h->err_word.release();
     h->tickets.release();
+    h->mtp.release();
     h->h_logits.release();
     h->h_hist.release();
     h->h_off.release();
@@ -501,6 +503,58 @@ int tqfs_apply_penalties(tqfs_handle* h, const void* logits_dev, int dtype, int 
     cudaError_t e = tqfs::launch_penalties(logits_dev, dtype, rows, vocab, ld, hist_dev, hist_off_dev,
                                            params_dev, out_dev, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "penalties launch");
+}
+
+int tqfs_mtp_verify(tqfs_handle* h, const void* target_dev, const void* draft_dev, int dtype,
+                    int seqs, int draft_len, int vocab, int64_t ld, const int32_t* drafts_dev,
+                    const tqfs_params* params_dev, const float* uniforms_dev,
+                    int32_t* out_accepted_dev, int32_t* out_token_dev, uint8_t* out_mask_dev,
+                    int32_t* out_status_dev, void* stream) {
+    if (!h) return TQFS_ERR_INVALID_ARG;
+    if (dtype != TQFS_DTYPE_F32 && dtype != TQFS_DTYPE_BF16)
+        return fail(h, TQFS_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+    if (seqs < 0 || draft_len < 0 || vocab <= 0 || ld < vocab)
+        return fail(h, TQFS_ERR_INVALID_ARG, "seqs=%d draft_len=%d vocab=%d ld=%lld", seqs, draft_len,
+                    vocab, static_cast<long long>(ld));
+    if (seqs == 0) return TQFS_OK;
+    if (!target_dev || !params_dev || !uniforms_dev || !out_accepted_dev || !out_token_dev ||
+        (draft_len > 0 && (!draft_dev || !drafts_dev)))
+        return fail(h, TQFS_ERR_INVALID_ARG, "NULL argument");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    const int ctas = seqs < 64 ? seqs : 64;
+    size_t stride = 0, key_stride = 0;
+    const size_t bytes = tqfs::mtp_scratch_bytes(vocab, ctas, &stride, &key_stride);
+    cudaError_t e = h->mtp.reserve(bytes);
+    if (e != cudaSuccess) return cuda_fail(h, e, "MTP scratch allocation");
+    tqfs::MtpScratch g;
+    g.stride = stride;
+    g.key_stride = key_stride;
+    unsigned char* b = static_cast<unsigned char*>(h->mtp.ptr);
+    g.work = reinterpret_cast<float*>(b);
+    g.e = reinterpret_cast<float*>(b + static_cast<size_t>(ctas) * 2 * stride * 4);
+    g.keys = reinterpret_cast<unsigned long long*>(b + static_cast<size_t>(ctas) * 2 * stride * 8);
+    tqfs::MtpArgs m;
+    m.target = target_dev;
+    m.draft = draft_dev;
+    m.dtype = dtype;
+    m.seqs = seqs;
+    m.draft_len = draft_len;
+    m.vocab = vocab;
+    m.ld = ld;
+    m.drafts = drafts_dev;
+    m.params = params_dev;
+    m.uniforms = uniforms_dev;
+    m.out_accepted = out_accepted_dev;
+    m.out_token = out_token_dev;
+    m.out_mask = out_mask_dev;
+    m.out_status = out_status_dev;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    {
+        TimingScope ts(h, s, 3);
+        e = tqfs::launch_mtp(m, g, ctas, s);
+    }
+    return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "MTP verify launch");
 }
 
 // ---- drop-in Sampler -------------------------------------------------------

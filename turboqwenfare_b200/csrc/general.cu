@@ -21,12 +21,13 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "filter.cuh"
 #include "internal.h"
 
 namespace tqfs {
 namespace {
 
-constexpr int kGenThreads = 512;
+constexpr int kGenThreads = kFilterThreads;
 
 // Rows the stream path does not own (row_mode in common.cuh).
 __device__ __forceinline__ bool is_general(const SampleArgs& a, int row, const tqfs_params& p) {
@@ -38,54 +39,11 @@ __device__ __forceinline__ bool is_general(const SampleArgs& a, int row, const t
     return row_mode(p, hs, he, a.hist_off != nullptr, a.vocab, false, &ws, &wl) == kModeGeneral;
 }
 
-__device__ __forceinline__ float block_max(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float m = red[0];
-    for (int w = 1; w < kGenThreads / 32; ++w) m = fmaxf(m, red[w]);
-    return m;
-}
-
-// Descending bitonic sort of n2 (a power of two) keys in global memory.
-__device__ void bitonic_desc(unsigned long long* keys, int n2) {
-    for (int size = 2; size <= n2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < (n2 >> 1); i += kGenThreads) {
-                const int lo = 2 * i - (i & (stride - 1));
-                const int hi = lo + stride;
-                const bool desc = (lo & size) == 0;
-                const unsigned long long a = keys[lo], b = keys[hi];
-                if ((a < b) == desc) {
-                    keys[lo] = b;
-                    keys[hi] = a;
-                }
-            }
-            __syncthreads();
-        }
-    }
-}
-
-__device__ __forceinline__ int pow2_at_least(int n) {
-    int p = 1;
-    while (p < n) p <<= 1;
-    return p;
-}
-
-template <int DT>
-__device__ __forceinline__ float logit_at(const void* logits, size_t base, int i) {
-    if constexpr (DT == 0) return static_cast<const float*>(logits)[base + i];
-    else return bf16_bits_to_f32(static_cast<const unsigned short*>(logits)[base + i]);
-}
-
 template <int DT>
 __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, GeneralScratch g) {
     __shared__ float red[kGenThreads / 32];
     __shared__ int sh_int[4];
-    __shared__ float sh_f[2];
+    __shared__ FilterOut fo;
     const int tid = threadIdx.x;
     const int V = a.vocab;
     float* W = g.work + static_cast<size_t>(blockIdx.x) * g.stride;
@@ -140,111 +98,26 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
             }
             __syncthreads();
         }
-        // ---- apply_top_k (mod.rs:153-161): pinned (value desc, id asc) ----
-        const uint32_t k = p.top_k;
-        const bool topk = k != 0u && k < static_cast<uint32_t>(V);
-        const int nc = topk ? static_cast<int>(k) : V;
-        if (topk) {
-            const int n2 = pow2_at_least(V);
-            for (int i = tid; i < n2; i += kGenThreads)
-                K[i] = i < V ? make_key(order32(W[i]), static_cast<uint32_t>(i)) : 0ull;
-            __syncthreads();
-            bitonic_desc(K, n2);
-            // candidate j: token key_token(K[j]), value key_value(K[j])
-        }
-        // ---- softmax (mod.rs:166-190) -------------------------------------
-        float lmax = -INFINITY;
-        for (int j = tid; j < nc; j += kGenThreads) {
-            const float v = topk ? key_value(K[j]) : W[j];
-            lmax = fmaxf(lmax, v);  // NaN never wins, as f32::max
-        }
-        const float mx = block_max(lmax, red);
-        for (int j = tid; j < nc; j += kGenThreads) {
-            const float v = topk ? key_value(K[j]) : W[j];
-            E[j] = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
-        }
-        __syncthreads();
+        // ---- top_k, softmax, top_p, min_p (mod.rs:153-224) ---------------
+        filter_row(W, E, K, V, p, red, &fo);
+        // ---- draw (mod.rs:227-248) ----------------------------------------
         if (tid == 0) {
-            float total = -0.0f;
-            int j = 0;
-            for (; j + 8 <= nc; j += 8) {
-                float x[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) x[q] = E[j + q];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) total = __fadd_rn(total, x[q]);
-            }
-            for (; j < nc; ++j) total = __fadd_rn(total, E[j]);
-            sh_f[0] = total;
-        }
-        __syncthreads();
-        const float total = sh_f[0];
-        const int n2 = pow2_at_least(nc);
-        // Candidate tokens go to W (dead once E is computed) so that K can be
-        // rewritten with probability keys.
-        unsigned int* tokens = reinterpret_cast<unsigned int*>(W);
-        for (int j = tid; j < nc; j += kGenThreads)
-            tokens[j] = topk ? key_token(K[j]) : static_cast<uint32_t>(j);
-        __syncthreads();
-        for (int j = tid; j < n2; j += kGenThreads) {
-            unsigned long long key = 0ull;
-            if (j < nc) {
-                const float e = E[j];
-                const float pj = total > 0.0f ? __fdiv_rn(e, total) : e;
-                key = make_key(order32(pj), tokens[j]);
-            }
-            K[j] = key;
-        }
-        __syncthreads();
-        bitonic_desc(K, n2);
-        // ---- top_p, min_p, draw (mod.rs:195-248) --------------------------
-        if (tid == 0) {
-            int keep = nc;
-            if (!(p.top_p >= 1.0f)) {
-                float cum = 0.0f;
-                int n = 0;
-                for (int i = 0; i < nc; ++i) {
-                    cum = __fadd_rn(cum, key_value(K[i]));
-                    ++n;
-                    if (cum >= p.top_p) break;
-                }
-                keep = n < 1 ? 1 : n;
-                if (keep > nc) keep = nc;
-            }
-            if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
-                const float floor = __fmul_rn(p.min_p, key_value(K[0]));
-                int n = 0;
-                while (n < keep && key_value(K[n]) >= floor) ++n;
-                keep = n < 1 ? 1 : n;
-            }
+            const int keep = fo.keep;
             int tok = 0;
             if (keep > 0) {
-                int pick = 0;
-                float total2 = -0.0f;
-                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, key_value(K[i]));
-                if (isfinite(total2) && total2 > 0.0f) {
-                    float u;
+                float u = 0.0f;
+                if (isfinite(fo.total2) && fo.total2 > 0.0f) {  // a uniform is consumed
                     if (a.uniforms != nullptr) {
                         u = a.uniforms[row];
                     } else {
-                        uint64_t s[4];
+                        uint64_t s4[4];
                         uint64_t* st = a.rng_state + static_cast<size_t>(row) * 4;
-                        for (int q = 0; q < 4; ++q) s[q] = st[q];
-                        u = xoshiro_next_f32(s);
-                        for (int q = 0; q < 4; ++q) st[q] = s[q];
-                    }
-                    const float target = __fmul_rn(u, total2);
-                    float cum = 0.0f;
-                    pick = keep - 1;
-                    for (int i = 0; i < keep; ++i) {
-                        cum = __fadd_rn(cum, key_value(K[i]));
-                        if (cum >= target) {
-                            pick = i;
-                            break;
-                        }
+                        for (int q = 0; q < 4; ++q) s4[q] = st[q];
+                        u = xoshiro_next_f32(s4);
+                        for (int q = 0; q < 4; ++q) st[q] = s4[q];
                     }
                 }
-                tok = static_cast<int>(key_token(K[pick]));
+                tok = draw_kept(K, keep, fo.total2, u);
             }
             sh_int[0] = tok;
             sh_int[1] = keep;

@@ -54,6 +54,33 @@ struct GeneralScratch {
     size_t key_stride;         // keys per CTA (a power of two >= vocab)
 };
 
+// Arguments of one MTP verify launch (device pointers).
+struct MtpArgs {
+    const void* target;        // seqs x (draft_len + 1) rows
+    const void* draft;         // seqs x draft_len rows
+    int dtype;
+    int seqs;
+    int draft_len;
+    int vocab;
+    long long ld;
+    const int32_t* drafts;     // seqs x draft_len draft tokens
+    const tqfs_params* params; // seqs
+    const float* uniforms;     // seqs x (draft_len + 1)
+    int32_t* out_accepted;     // seqs
+    int32_t* out_token;        // seqs
+    uint8_t* out_mask;         // seqs x draft_len, optional
+    int32_t* out_status;       // seqs, optional
+};
+
+// Two row workspaces per CTA of the MTP kernel (library scratch).
+struct MtpScratch {
+    float* work;               // logits, then candidate tokens
+    float* e;                  // exponentials
+    unsigned long long* keys;  // probability keys, then residual lists
+    size_t stride;             // floats per workspace in work / e
+    size_t key_stride;         // keys per list (a power of two >= vocab)
+};
+
 struct Plan {
     int chunks;
     int chunk_len;
@@ -77,6 +104,8 @@ cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int cta
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,
                              const int32_t* hist, const int64_t* hist_off,
                              const tqfs_params* params, float* out, cudaStream_t s);
+size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
+cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s);
 cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,
                               tqfs_candidate* out_top4, cudaStream_t s);
 

@@ -1,8 +1,10 @@
-"""MTP verification: greedy `verify_pair`, statistics and controller.
+"""MTP verification: greedy `verify_pair`, statistics and controller, and the
+batched device verify.
 
-Host-side mirror of src/runtime/mtp.rs:47-168. The batched device verify
-(stochastic speculative sampling over post-filter distributions) is exposed
-by `mtp_verify` once the library provides it.
+Host-side mirror of src/runtime/mtp.rs:47-168. `verify_batch` runs
+`tqfs_mtp_verify`: the greedy rule of verify_pair for temperature-0
+sequences, and speculative sampling over the sampler's post-filter
+distributions for sampled ones (the rule is documented in include/tqfs.h).
 """
 from __future__ import annotations
 
@@ -85,3 +87,46 @@ class MtpController:
         elif self._enabled and rolling < self.disable_threshold:
             self._enabled = False
         return self._enabled
+
+
+@dataclass
+class MtpBatchResult:
+    """Per sequence: drafts accepted (0..L), the token to append, the status
+    (0 ok, 2 unsupported: active penalty); mask: every position's decision."""
+
+    accepted: "object"
+    token: "object"
+    mask: "object"
+    status: "object"
+
+
+def verify_batch(target, draft, drafts, params, uniforms, vocab=None, handle=None) -> MtpBatchResult:
+    """Device MTP verify over CUDA tensors.
+
+    target: (seqs, L+1, ld) float32/bfloat16; draft: (seqs, L, ld) of the same
+    dtype; drafts: (seqs, L) int32; params: one tqfs_params per sequence
+    (numpy PARAMS_DTYPE array, SamplingParams list or packed uint8 tensor);
+    uniforms: (seqs, L+1) float32 on the 2^-24 grid.
+    """
+    import torch
+    from . import _native as N
+    from .sampler import params_tensor, _ptr, _stream
+
+    seqs, L1, ld = target.shape
+    L = L1 - 1
+    dev = target.device
+    h = handle or N.default_handle(dev.index or 0)
+    dtype = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16}.get(target.dtype)
+    if dtype is None or draft.dtype != target.dtype:
+        raise N.TqfsError(N.ERR_UNSUPPORTED_DTYPE, str(target.dtype))
+    if not (isinstance(params, torch.Tensor) and params.dtype == torch.uint8):
+        params = params_tensor(params, seqs, dev)
+    acc = torch.empty(seqs, dtype=torch.int32, device=dev)
+    tok = torch.empty(seqs, dtype=torch.int32, device=dev)
+    mask = torch.empty((seqs, max(L, 1)), dtype=torch.uint8, device=dev)
+    status = torch.empty(seqs, dtype=torch.int32, device=dev)
+    n = ld if vocab is None else vocab
+    h.check(N.lib().tqfs_mtp_verify(
+        h.ptr, _ptr(target), _ptr(draft), dtype, seqs, L, n, ld, _ptr(drafts), _ptr(params),
+        _ptr(uniforms), _ptr(acc), _ptr(tok), _ptr(mask), _ptr(status), _stream(dev)))
+    return MtpBatchResult(acc, tok, mask[:, :L], status)

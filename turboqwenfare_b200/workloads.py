@@ -189,3 +189,51 @@ def config(name: str, rows: Optional[int] = None, vocab: int = V_DEFAULT, seed: 
         hist, off = _histories(rng, [4096] * n, vocab)
         return Batch(name, logits, params, hist, off, philox_uniforms(seed + 4, n), "bf16")
     raise ValueError(f"unknown config {name}")
+
+
+@dataclass
+class MtpBatch:
+    """Configuration 3: MTP verify inputs. target: seqs x (L+1) x vocab,
+    draft: seqs x L x vocab (f32), drafts: seqs x L, uniforms: seqs x (L+1)."""
+
+    name: str
+    target: np.ndarray
+    draft: np.ndarray
+    drafts: np.ndarray
+    params: np.ndarray
+    uniforms: np.ndarray
+
+    @property
+    def seqs(self) -> int:
+        return self.target.shape[0]
+
+    @property
+    def draft_len(self) -> int:
+        return self.draft.shape[1]
+
+    def algorithmic_bytes(self) -> int:
+        """Target and draft logits read once."""
+        return int(self.target.nbytes + self.draft.nbytes)
+
+
+def mtp_config(seqs: int = 32, draft_len: int = 3, vocab: int = V_DEFAULT, seed: int = 0,
+               temperature: float = 0.8, top_p: float = 0.9, top_k: int = 0) -> MtpBatch:
+    """Target logits as configuration 0 (2.5 N(0,1) + Zipf bias), draft =
+    target + 0.5 N(0,1). Draft tokens are drawn from the draft's softmax at
+    `temperature` over its 256 largest logits with seeded uniforms (input
+    generation, not the sampler under test)."""
+    rng = np.random.default_rng([seed, zlib.crc32(b"c3")])
+    rows = seqs * (draft_len + 1)
+    target = zipf_logits(rng, rows, vocab).reshape(seqs, draft_len + 1, vocab)
+    draft = (target[:, :draft_len, :] + 0.5 * rng.standard_normal((seqs, draft_len, vocab))).astype(np.float32)
+    drafts = np.zeros((seqs, draft_len), np.int32)
+    for s in range(seqs):
+        for j in range(draft_len):
+            row = draft[s, j]
+            top = np.argpartition(row, -256)[-256:]
+            z = row[top].astype(np.float64) / max(temperature, 1e-3)
+            w = np.exp(z - z.max())
+            drafts[s, j] = int(rng.choice(top, p=w / w.sum()))
+    params = params_rows(seqs, temperature, top_p=top_p, top_k=top_k)
+    u = philox_uniforms(seed + 3, seqs * (draft_len + 1)).reshape(seqs, draft_len + 1)
+    return MtpBatch("c3", target, draft, drafts, params, u)
