@@ -219,6 +219,48 @@ int tqfs_mtp_verify(tqfs_handle* handle, const void* target_dev, const void* dra
                     int32_t* out_accepted_dev, int32_t* out_token_dev, uint8_t* out_mask_dev,
                     int32_t* out_status_dev, void* stream);
 
+/* ---- vocabulary-sharded sampling (configuration 4) ----------------------- */
+/*
+ * A row's vocabulary split over ranks: rank r holds ids [vocab_offset,
+ * vocab_offset + vocab_local) of vocab_total. Histories, params and uniforms
+ * are replicated (global ids). Each rank exports, per row, its exact top-k by
+ * (value desc, id asc) after penalties (sampled rows with 0 < top_k <= 128),
+ * or its top-4 (greedy rows), as keys with global ids; the records of all
+ * ranks are all-gathered; every rank merges them into the row's top-k (which
+ * always lies in the union of the ranks' top-k) and draws exactly as
+ * tqfs_sample would on the whole row, so all ranks return the same tokens.
+ * Rows needing the whole vocabulary (top_k 0 or > 128, or a penalty window
+ * above 8,192 tokens) get TQFS_ROW_ERR_UNSUPPORTED and token -1.
+ * No counterpart in the reference (its sampler runs on one host).
+ */
+/* u64 words per row in a rank's record. */
+int tqfs_shard_record_words(void);
+/* This rank's records: rec_dev holds rows x tqfs_shard_record_words() u64. */
+int tqfs_shard_export(tqfs_handle* handle, const void* logits_dev, int dtype, int rows,
+                      int vocab_local, int64_t ld, int vocab_offset, int vocab_total,
+                      const int32_t* hist_dev, const int64_t* hist_off_dev,
+                      const tqfs_params* params_dev, uint64_t* rec_dev, void* stream);
+/* Merge all ranks' records (rank r's rows at recs_dev + r * rows * words) and
+ * draw: out_token_dev / out_status_dev per row. */
+int tqfs_shard_merge(tqfs_handle* handle, const uint64_t* recs_dev, int nranks, int rows,
+                     int vocab_total, const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                     const float* uniforms_dev, uint64_t* rng_state_dev, int32_t* out_token_dev,
+                     int32_t* out_status_dev, void* stream);
+/* NCCL (libnccl.so.2, loaded at run time): a 128-byte unique id made on one
+ * rank and shared by the caller, one communicator per rank on the handle's
+ * device. */
+int tqfs_nccl_unique_id(void* id_out);
+int tqfs_nccl_comm_init(tqfs_handle* handle, int nranks, int rank, const void* id, void** comm_out);
+int tqfs_nccl_comm_destroy(void* comm);
+/* Export, ncclAllGather over the communicator, merge: one call per rank, on
+ * `stream`. */
+int tqfs_sample_vocab_sharded(tqfs_handle* handle, void* comm, int nranks, const void* logits_dev,
+                              int dtype, int rows, int vocab_local, int64_t ld, int vocab_offset,
+                              int vocab_total, const int32_t* hist_dev,
+                              const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                              const float* uniforms_dev, uint64_t* rng_state_dev,
+                              int32_t* out_token_dev, int32_t* out_status_dev, void* stream);
+
 /*
  * tqfs_sample without any GPU allocation. No counterpart in the reference
  * (its sampler is host code); it exists for callers that cannot call

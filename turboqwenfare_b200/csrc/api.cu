@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <dlfcn.h>
 #include <mutex>
 #include <new>
 #include <string>
@@ -55,6 +56,8 @@ struct tqfs_handle {
     DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
     DeviceBuffer tickets;      // per-row unit tickets, tagged with the call's number
     DeviceBuffer mtp;          // MTP verify workspaces
+    DeviceBuffer shard_send;   // this shard's records for the all-gather
+    DeviceBuffer shard_recv;   // every shard's records
     uint32_t epoch = 0;        // number of the last call
     size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
@@ -178,6 +181,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     if (a.rows == 0) return TQFS_OK;
+    if (a.vocab_route == 0) a.vocab_route = a.vocab;  // not a shard
     if (a.vocab == 0) {
         cudaError_t e = tqfs::launch_fill_empty(a.rows, a.out_token, a.out_status, a.out_top4, s);
         return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "launch");
@@ -304,6 +308,8 @@ int tqfs_destroy(tqfs_handle* h) {
     h->err_word.release();
     h->tickets.release();
     h->mtp.release();
+    h->shard_send.release();
+    h->shard_recv.release();
     h->h_logits.release();
     h->h_hist.release();
     h->h_off.release();
@@ -555,6 +561,191 @@ int tqfs_mtp_verify(tqfs_handle* h, const void* target_dev, const void* draft_de
         e = tqfs::launch_mtp(m, g, ctas, s);
     }
     return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "MTP verify launch");
+}
+
+// ---- vocabulary shards ------------------------------------------------------
+
+int tqfs_shard_record_words(void) { return tqfs::kShardRec; }
+
+int tqfs_shard_export(tqfs_handle* h, const void* logits_dev, int dtype, int rows, int vocab_local,
+                      int64_t ld, int vocab_offset, int vocab_total, const int32_t* hist_dev,
+                      const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                      uint64_t* rec_dev, void* stream) {
+    int st = check_common(h, logits_dev, dtype, rows, vocab_local, ld);
+    if (st != TQFS_OK) return st;
+    if (rows == 0) return TQFS_OK;
+    if (vocab_local <= 0 || vocab_offset < 0 || vocab_total < vocab_offset + vocab_local || !params_dev ||
+        !rec_dev || (hist_off_dev && !hist_dev))
+        return fail(h, TQFS_ERR_INVALID_ARG, "shard [%d, %d) of %d", vocab_offset, vocab_offset + vocab_local,
+                    vocab_total);
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    tqfs::SampleArgs a{};
+    a.logits = logits_dev;
+    a.dtype = dtype;
+    a.rows = rows;
+    a.vocab = vocab_local;
+    a.ld = ld;
+    a.hist = hist_dev;
+    a.hist_off = hist_off_dev;
+    a.params = params_dev;
+    a.vocab_route = vocab_total;
+    a.vocab_offset = vocab_offset;
+    a.export_rec = reinterpret_cast<unsigned long long*>(rec_dev);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const tqfs::Plan plan = tqfs::plan_stream(a.rows, a.vocab, a.dtype);
+    if (plan.chunks == 0) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
+    if ((st = ensure_scratch(h, a.rows, plan, a)) != TQFS_OK) return st;
+    const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
+    a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
+    cudaError_t e;
+    {
+        TimingScope ts(h, s, 2);
+        e = tqfs::launch_window(a, plan, s);
+    }
+    if (e == cudaSuccess) {
+        TimingScope ts(h, s, 0);
+        e = tqfs::launch_stream(a, plan, s, hist_off_dev != nullptr && !h->timing);
+    }
+    return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "shard export launch");
+}
+
+int tqfs_shard_merge(tqfs_handle* h, const uint64_t* recs_dev, int nranks, int rows, int vocab_total,
+                     const int64_t* hist_off_dev, const tqfs_params* params_dev,
+                     const float* uniforms_dev, uint64_t* rng_state_dev, int32_t* out_token_dev,
+                     int32_t* out_status_dev, void* stream) {
+    if (!h) return TQFS_ERR_INVALID_ARG;
+    if (rows < 0 || nranks <= 0 || vocab_total <= 0) return fail(h, TQFS_ERR_INVALID_ARG, "rows/nranks/vocab");
+    if (rows == 0) return TQFS_OK;
+    if (!recs_dev || !params_dev || !out_token_dev || (!uniforms_dev && !rng_state_dev))
+        return fail(h, TQFS_ERR_INVALID_ARG, "NULL argument");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    tqfs::MergeArgs m;
+    m.recs = reinterpret_cast<const unsigned long long*>(recs_dev);
+    m.nranks = nranks;
+    m.rows = rows;
+    m.vocab_total = vocab_total;
+    m.hist_off = hist_off_dev;
+    m.params = params_dev;
+    m.uniforms = uniforms_dev;
+    m.rng_state = rng_state_dev;
+    m.out_token = out_token_dev;
+    m.out_status = out_status_dev;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        TimingScope ts(h, s, 1);
+        e = tqfs::launch_merge(m, s);
+    }
+    return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "shard merge launch");
+}
+
+namespace {
+
+// NCCL, loaded at run time: the process's own libnccl.so.2 when one is
+// already loaded (a framework's), else the system's. Only the entry points
+// below are used; their C ABI is NCCL's stable one.
+typedef struct {
+    char internal[128];
+} NcclUniqueId;
+using NcclComm = void*;
+enum { kNcclSuccess = 0, kNcclUint64 = 5 };
+struct NcclApi {
+    bool tried = false;
+    void* dl = nullptr;
+    int (*get_unique_id)(NcclUniqueId*) = nullptr;
+    int (*comm_init_rank)(NcclComm*, int, NcclUniqueId, int) = nullptr;
+    int (*all_gather)(const void*, void*, size_t, int, NcclComm, cudaStream_t) = nullptr;
+    int (*comm_destroy)(NcclComm) = nullptr;
+    const char* (*error_string)(int) = nullptr;
+};
+std::mutex g_nccl_mutex;
+NcclApi g_nccl;
+
+const NcclApi* nccl() {
+    std::lock_guard<std::mutex> lock(g_nccl_mutex);
+    if (!g_nccl.tried) {
+        g_nccl.tried = true;
+        void* dl = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (dl != nullptr) {
+            g_nccl.get_unique_id = reinterpret_cast<int (*)(NcclUniqueId*)>(dlsym(dl, "ncclGetUniqueId"));
+            g_nccl.comm_init_rank =
+                reinterpret_cast<int (*)(NcclComm*, int, NcclUniqueId, int)>(dlsym(dl, "ncclCommInitRank"));
+            g_nccl.all_gather = reinterpret_cast<int (*)(const void*, void*, size_t, int, NcclComm, cudaStream_t)>(
+                dlsym(dl, "ncclAllGather"));
+            g_nccl.comm_destroy = reinterpret_cast<int (*)(NcclComm)>(dlsym(dl, "ncclCommDestroy"));
+            g_nccl.error_string = reinterpret_cast<const char* (*)(int)>(dlsym(dl, "ncclGetErrorString"));
+            if (g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_gather && g_nccl.comm_destroy &&
+                g_nccl.error_string)
+                g_nccl.dl = dl;
+        }
+    }
+    return g_nccl.dl != nullptr ? &g_nccl : nullptr;
+}
+
+int nccl_fail(tqfs_handle* h, const NcclApi* n, int r, const char* what) {
+    return fail(h, TQFS_ERR_NCCL, "%s: %s", what, n->error_string(r));
+}
+
+}  // namespace
+
+int tqfs_nccl_unique_id(void* id_out) {
+    const NcclApi* n = nccl();
+    if (n == nullptr) return TQFS_ERR_NCCL;
+    if (id_out == nullptr) return TQFS_ERR_INVALID_ARG;
+    NcclUniqueId id;
+    if (n->get_unique_id(&id) != kNcclSuccess) return TQFS_ERR_NCCL;
+    std::memcpy(id_out, &id, sizeof(id));
+    return TQFS_OK;
+}
+
+int tqfs_nccl_comm_init(tqfs_handle* h, int nranks, int rank, const void* id, void** comm_out) {
+    if (!h || !id || !comm_out || nranks <= 0 || rank < 0 || rank >= nranks) return TQFS_ERR_INVALID_ARG;
+    *comm_out = nullptr;
+    const NcclApi* n = nccl();
+    if (n == nullptr) return fail(h, TQFS_ERR_NCCL, "libnccl.so.2 not found");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    NcclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    NcclComm c = nullptr;
+    const int r = n->comm_init_rank(&c, nranks, uid, rank);
+    if (r != kNcclSuccess) return nccl_fail(h, n, r, "ncclCommInitRank");
+    *comm_out = c;
+    return TQFS_OK;
+}
+
+int tqfs_nccl_comm_destroy(void* comm) {
+    const NcclApi* n = nccl();
+    if (n == nullptr || comm == nullptr) return TQFS_ERR_INVALID_ARG;
+    return n->comm_destroy(comm) == kNcclSuccess ? TQFS_OK : TQFS_ERR_NCCL;
+}
+
+int tqfs_sample_vocab_sharded(tqfs_handle* h, void* comm, int nranks, const void* logits_dev, int dtype,
+                              int rows, int vocab_local, int64_t ld, int vocab_offset, int vocab_total,
+                              const int32_t* hist_dev, const int64_t* hist_off_dev,
+                              const tqfs_params* params_dev, const float* uniforms_dev,
+                              uint64_t* rng_state_dev, int32_t* out_token_dev, int32_t* out_status_dev,
+                              void* stream) {
+    if (!h || !comm || nranks <= 0) return TQFS_ERR_INVALID_ARG;
+    if (rows == 0) return TQFS_OK;
+    const NcclApi* n = nccl();
+    if (n == nullptr) return fail(h, TQFS_ERR_NCCL, "libnccl.so.2 not found");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    const size_t words = static_cast<size_t>(rows) * tqfs::kShardRec;
+    cudaError_t e = h->shard_send.reserve(words * 8);
+    if (e == cudaSuccess) e = h->shard_recv.reserve(words * 8 * nranks);
+    if (e != cudaSuccess) return cuda_fail(h, e, "shard buffers");
+    uint64_t* send = static_cast<uint64_t*>(h->shard_send.ptr);
+    uint64_t* recv = static_cast<uint64_t*>(h->shard_recv.ptr);
+    st = tqfs_shard_export(h, logits_dev, dtype, rows, vocab_local, ld, vocab_offset, vocab_total, hist_dev,
+                           hist_off_dev, params_dev, send, stream);
+    if (st != TQFS_OK) return st;
+    const int r = n->all_gather(send, recv, words, kNcclUint64, comm, static_cast<cudaStream_t>(stream));
+    if (r != kNcclSuccess) return nccl_fail(h, n, r, "ncclAllGather");
+    return tqfs_shard_merge(h, recv, nranks, rows, vocab_total, hist_off_dev, params_dev, uniforms_dev,
+                            rng_state_dev, out_token_dev, out_status_dev, stream);
 }
 
 // ---- drop-in Sampler -------------------------------------------------------

@@ -25,6 +25,7 @@ constexpr int kStreamMaxK = 128;     // largest top_k the stream path owns
 constexpr int kChunkCap = 256;       // candidate keys kept per (row, chunk)
 constexpr int kWinCap = 8192;        // penalty-window tokens the stream path buckets
 constexpr int kMaxChunks = 512;      // chunks per row (8 KiB of logits each)
+constexpr int kShardRec = 2 + kStreamMaxK;  // u64 per row in a vocabulary shard's record
 
 // Which kernel owns a row.
 enum : int { kModeGreedy = 0, kModeStream = 1, kModeGeneral = 2 };

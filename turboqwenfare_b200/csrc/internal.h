@@ -41,6 +41,9 @@ struct SampleArgs {
     uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
     uint32_t epoch;            // this call's number (never 0)
     int vec_ok;                // rows start on 16-byte boundaries
+    int vocab_route;           // vocabulary the routing compares top_k with
+    int vocab_offset;          // global id of this shard's first id
+    unsigned long long* export_rec;  // rows x kShardRec: export mode (a shard)
     int top4_only;             // tqfs_top_logit_candidates: every row is greedy
 };
 
@@ -70,6 +73,20 @@ struct MtpArgs {
     int32_t* out_token;        // seqs
     uint8_t* out_mask;         // seqs x draft_len, optional
     int32_t* out_status;       // seqs, optional
+};
+
+// Merge of all_gathered vocabulary-shard records (device pointers).
+struct MergeArgs {
+    const unsigned long long* recs;  // nranks x rows x kShardRec
+    int nranks;
+    int rows;
+    int vocab_total;
+    const int64_t* hist_off;
+    const tqfs_params* params;
+    const float* uniforms;
+    uint64_t* rng_state;
+    int32_t* out_token;
+    int32_t* out_status;
 };
 
 // Two row workspaces per CTA of the MTP kernel (library scratch).
@@ -104,6 +121,7 @@ cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int cta
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,
                              const int32_t* hist, const int64_t* hist_off,
                              const tqfs_params* params, float* out, cudaStream_t s);
+cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s);
 size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
 cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s);
 cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,

@@ -129,6 +129,7 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     a.vec_ok = (reinterpret_cast<uintptr_t>(logits_dev) & 15u) == 0 &&
                (static_cast<size_t>(ld) * esz) % 16 == 0;
     a.top4_only = 0;
+    a.vocab_route = vocab;
 
     mark_unhandled_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token_dev, out_status_dev);
     if (cudaGetLastError() != cudaSuccess) return TQFS_ERR_CUDA;

@@ -61,6 +61,7 @@ constexpr int kSortOff = kBinsOff + 256 * 4;       // ranked keys of a finalised
 constexpr int kWarpSmem = kSortOff + kStreamMaxK * 8;  // 21 KiB
 constexpr int kCasTries = 1 << 20;                 // attempts at a row ticket
 constexpr int kMaxUnits = 32;                      // units per row (one lane each)
+constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
 constexpr int kWinWarps = 8;      // warps of the window kernel
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
@@ -274,7 +275,7 @@ __device__ __forceinline__ Info decode(unsigned long long w, Pos p, const Info& 
         static_assert(sizeof(tqfs_params) == 40, "tqfs_params layout");
         memcpy(&prm, pw, sizeof(prm));
         long long ws, wl;
-        f.mode = row_mode(prm, hs, he, a.hist_off != nullptr, a.vocab, a.top4_only != 0, &ws, &wl);
+        f.mode = row_mode(prm, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
         f.k = static_cast<int>(prm.top_k);
         f.unit_pen = f.mode == kModeStream && wl > 0;
         f.pn = Pen{prm.repeat_penalty, prm.frequency_penalty, prm.presence_penalty};
@@ -635,13 +636,104 @@ __device__ __forceinline__ void warp_rank_sort(const unsigned long long* src, in
     __syncwarp();
 }
 
+// The exact top-k by (value desc, id asc) of the n candidate keys L[0..n)
+// (a set that contains the row's top-k), then softmax, top_p, min_p and the
+// inverse-CDF draw exactly as src/sampling/mod.rs:166-248 does, the
+// sequential f32 sums in order by one lane. Returns the token (every lane);
+// with out_probs_row, writes the kept probabilities at their tokens. L (any
+// size up to kListCap) and S (kStreamMaxK keys) are the warp's shared memory.
+__device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned long long* L,
+                                           int n, unsigned long long* S, unsigned int* bins,
+                                           const float* uniforms, uint64_t* rng_state, int row,
+                                           float* out_probs_row) {
+    const int lane = threadIdx.x & 31;
+    warp_keep_top(L, &n, k, bins);
+    const int kk = n;  // min(k, candidates)
+    warp_rank_sort(L, kk, S);
+    // softmax over the survivors (src/sampling/mod.rs:166-190)
+    float* E = reinterpret_cast<float*>(L);                                  // kk floats
+    unsigned long long* PK = L + kStreamMaxK / 2;                           // kk keys
+    float* P = reinterpret_cast<float*>(L + kStreamMaxK / 2 + kStreamMaxK);  // kk floats
+    const float first = kk > 0 ? key_value(S[0]) : 0.0f;
+    const float mx = (kk > 0 && first == first) ? first : -INFINITY;
+    for (int i = lane; i < kk; i += 32)
+        E[i] = exp_f32(__fdiv_rn(__fsub_rn(key_value(S[i]), mx), p.temperature));
+    __syncwarp();
+    float total_e = -0.0f;
+    if (lane == 0)
+        for (int i = 0; i < kk; ++i) total_e = __fadd_rn(total_e, E[i]);
+    total_e = __shfl_sync(0xFFFFFFFFu, total_e, 0);
+    for (int i = lane; i < kk; i += 32) {
+        const float pv = total_e > 0.0f ? __fdiv_rn(E[i], total_e) : E[i];
+        PK[i] = make_key(order32(pv), key_token(S[i]));
+    }
+    __syncwarp();
+    warp_rank_sort(PK, kk, S);  // probability keys in draw order
+    for (int i = lane; i < kk; i += 32) P[i] = key_value(S[i]);
+    __syncwarp();
+    // top_p, min_p, draw (src/sampling/mod.rs:195-248)
+    int keep = kk, token = 0;
+    if (lane == 0) {
+        if (!(p.top_p >= 1.0f)) {
+            float cum = 0.0f;
+            int c = 0;
+            for (int i = 0; i < kk; ++i) {
+                cum = __fadd_rn(cum, P[i]);
+                ++c;
+                if (cum >= p.top_p) break;
+            }
+            keep = c < 1 ? 1 : c;
+            if (keep > kk) keep = kk;
+        }
+        if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
+            const float floor = __fmul_rn(p.min_p, P[0]);
+            int c = 0;
+            while (c < keep && P[c] >= floor) ++c;
+            keep = c < 1 ? 1 : c;
+        }
+        if (keep > 0) {
+            int pick = 0;
+            float total2 = -0.0f;
+            for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, P[i]);
+            if (isfinite(total2) && total2 > 0.0f) {
+                float u;
+                if (uniforms != nullptr) {
+                    u = uniforms[row];
+                } else {
+                    uint64_t st[4];
+                    uint64_t* sp = rng_state + static_cast<size_t>(row) * 4;
+                    for (int q = 0; q < 4; ++q) st[q] = sp[q];
+                    u = xoshiro_next_f32(st);
+                    for (int q = 0; q < 4; ++q) sp[q] = st[q];
+                }
+                const float target = __fmul_rn(u, total2);
+                float cum = 0.0f;
+                pick = keep - 1;
+                for (int i = 0; i < keep; ++i) {
+                    cum = __fadd_rn(cum, P[i]);
+                    if (cum >= target) {
+                        pick = i;
+                        break;
+                    }
+                }
+            }
+            token = static_cast<int>(key_token(S[pick]));
+        }
+    }
+    token = __shfl_sync(0xFFFFFFFFu, token, 0);
+    keep = __shfl_sync(0xFFFFFFFFu, keep, 0);
+    if (out_probs_row != nullptr)
+        for (int i = lane; i < keep; i += 32) out_probs_row[key_token(S[i])] = P[i];
+    __syncwarp();
+    return token;
+}
+
 // Finalises a row in one warp once all its units have written their lists:
 // greedy rows take the top-4 (src/runtime/decode.rs:48-64); sampled rows the
-// exact top-k by (value desc, id asc) of the union of the units' lists (every
-// row top-k member is in its unit's top-k), then softmax, top_p, min_p and
-// the inverse-CDF draw as src/sampling/mod.rs:166-248 does, the sequential
-// f32 sums in order by one lane. L (kListCap keys) and S (128 keys) are the
-// warp's shared memory.
+// union of the units' lists (every row top-k member is in its unit's top-k)
+// filtered by the largest unit k-th value, then finish_sampled. In export
+// mode (a vocabulary shard) it writes the row's exact top-k (sampled) or
+// top-4 (greedy) keys with global ids to the row's record instead.
 __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool greedy, int k,
                                           unsigned long long* L, unsigned long long* S,
                                           unsigned int* bins, int* counter) {
@@ -653,10 +745,16 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
     const int m_raw = (!greedy && lane < U) ? __ldcg(a.cand_n + base + lane) : 0;
     const uint32_t th_u = (!greedy && lane < U) ? __ldcg(a.theta + base + lane) : 0u;
     const tqfs_params p = greedy ? tqfs_params{} : a.params[row];
+    unsigned long long* rec = a.export_rec != nullptr ? a.export_rec + static_cast<size_t>(row) * kShardRec : nullptr;
+    const unsigned long long goff = static_cast<unsigned long long>(a.vocab_offset);
     int token = 0;
     const bool timed_out = *reinterpret_cast<volatile uint32_t*>(a.err_word) == a.epoch;
     if (timed_out) {  // the units' lists may be missing: report and stop
         if (lane == 0) {
+            if (rec != nullptr) {
+                rec[0] = 0ull;
+                rec[1] = 1ull;
+            }
             if (a.out_token != nullptr) a.out_token[row] = -1;
             if (a.out_status != nullptr) a.out_status[row] = TQFS_ROW_ERR_TIMEOUT;
         }
@@ -668,6 +766,15 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
         for (int i = lane; i < U * 4; i += 32) top4_insert(t, __ldcg(a.top4 + base * 4 + i));
         unsigned long long o[4];
         warp_top4(t, o, lane);
+        if (rec != nullptr && greedy) {
+            if (lane == 0) {
+                rec[0] = 4ull;
+                rec[1] = 0ull;
+                for (int r = 0; r < 4; ++r) rec[2 + r] = o[r] ? o[r] - goff : 0ull;
+            }
+            __syncwarp();
+            return;
+        }
         if (lane == 0 && a.out_top4 != nullptr) {
             for (int r = 0; r < 4; ++r) {
                 tqfs_candidate cnd;
@@ -713,92 +820,82 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
             n += __popc(ball);
             __syncwarp();
         }
-        warp_keep_top(L, &n, k, bins);
-        const int kk = n;  // min(k, survivors)
-        warp_rank_sort(L, kk, S);
-        // softmax over the survivors (src/sampling/mod.rs:166-190)
-        float* E = reinterpret_cast<float*>(L);                        // kk floats
-        unsigned long long* PK = L + kStreamMaxK / 2;                 // kk keys
-        float* P = reinterpret_cast<float*>(L + kStreamMaxK / 2 + kStreamMaxK);  // kk floats
-        const float first = kk > 0 ? key_value(S[0]) : 0.0f;
-        const float mx = (kk > 0 && first == first) ? first : -INFINITY;
-        for (int i = lane; i < kk; i += 32)
-            E[i] = exp_f32(__fdiv_rn(__fsub_rn(key_value(S[i]), mx), p.temperature));
-        __syncwarp();
-        float total_e = -0.0f;
-        if (lane == 0)
-            for (int i = 0; i < kk; ++i) total_e = __fadd_rn(total_e, E[i]);
-        total_e = __shfl_sync(0xFFFFFFFFu, total_e, 0);
-        for (int i = lane; i < kk; i += 32) {
-            const float pv = total_e > 0.0f ? __fdiv_rn(E[i], total_e) : E[i];
-            PK[i] = make_key(order32(pv), key_token(S[i]));
+        if (rec != nullptr) {  // export: the shard's exact top-k, global ids
+            warp_keep_top(L, &n, k, bins);
+            for (int i = lane; i < n; i += 32) rec[2 + i] = L[i] - goff;
+            if (lane == 0) {
+                rec[0] = static_cast<unsigned long long>(n);
+                rec[1] = 0ull;
+            }
+            __syncwarp();
+            return;
         }
-        __syncwarp();
-        warp_rank_sort(PK, kk, S);  // probability keys in draw order
-        for (int i = lane; i < kk; i += 32) P[i] = key_value(S[i]);
-        __syncwarp();
-        // top_p, min_p, draw (src/sampling/mod.rs:195-248)
-        int keep = kk;
-        if (lane == 0) {
-            if (!(p.top_p >= 1.0f)) {
-                float cum = 0.0f;
-                int c = 0;
-                for (int i = 0; i < kk; ++i) {
-                    cum = __fadd_rn(cum, P[i]);
-                    ++c;
-                    if (cum >= p.top_p) break;
-                }
-                keep = c < 1 ? 1 : c;
-                if (keep > kk) keep = kk;
-            }
-            if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
-                const float floor = __fmul_rn(p.min_p, P[0]);
-                int c = 0;
-                while (c < keep && P[c] >= floor) ++c;
-                keep = c < 1 ? 1 : c;
-            }
-            int tok = 0;
-            if (keep > 0) {
-                int pick = 0;
-                float total2 = -0.0f;
-                for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, P[i]);
-                if (isfinite(total2) && total2 > 0.0f) {
-                    float u;
-                    if (a.uniforms != nullptr) {
-                        u = a.uniforms[row];
-                    } else {
-                        uint64_t st[4];
-                        uint64_t* sp = a.rng_state + static_cast<size_t>(row) * 4;
-                        for (int q = 0; q < 4; ++q) st[q] = sp[q];
-                        u = xoshiro_next_f32(st);
-                        for (int q = 0; q < 4; ++q) sp[q] = st[q];
-                    }
-                    const float target = __fmul_rn(u, total2);
-                    float cum = 0.0f;
-                    pick = keep - 1;
-                    for (int i = 0; i < keep; ++i) {
-                        cum = __fadd_rn(cum, P[i]);
-                        if (cum >= target) {
-                            pick = i;
-                            break;
-                        }
-                    }
-                }
-                tok = static_cast<int>(key_token(S[pick]));
-            }
-            token = tok;
-        }
-        token = __shfl_sync(0xFFFFFFFFu, token, 0);
-        keep = __shfl_sync(0xFFFFFFFFu, keep, 0);
-        if (a.out_probs != nullptr)
-            for (int i = lane; i < keep; i += 32)
-                a.out_probs[static_cast<size_t>(row) * a.ld + key_token(S[i])] = P[i];
+        float* pr = a.out_probs != nullptr ? a.out_probs + static_cast<size_t>(row) * a.ld : nullptr;
+        token = finish_sampled(p, k, L, n, S, bins, a.uniforms, a.rng_state, row, pr);
     }
     if (lane == 0) {
         if (a.out_token != nullptr) a.out_token[row] = token;
         if (a.out_status != nullptr) a.out_status[row] = TQFS_ROW_OK;
     }
     __syncwarp();
+}
+
+// Merges the records of `nranks` vocabulary shards (all_gathered: rank r's
+// rows at recs + r * rows * kShardRec) and finalises every row, one warp per
+// row: greedy rows take the top-4 of the shards' top-4; sampled rows the
+// exact top-k of the union of the shards' top-k lists (the row's top-k is
+// always inside it), then finish_sampled. General rows (not shardable here)
+// get TQFS_ROW_ERR_UNSUPPORTED.
+__global__ void __launch_bounds__(kSW * 32) merge_kernel(MergeArgs m) {
+    extern __shared__ __align__(16) unsigned char mdyn[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned char* wbase = mdyn + static_cast<size_t>(warp) * kMergeSmem;
+    unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase);
+    unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + kListCap * 8);
+    unsigned long long* S = reinterpret_cast<unsigned long long*>(wbase + kListCap * 8 + 1024);
+    for (int row = blockIdx.x * kSW + warp; row < m.rows; row += gridDim.x * kSW) {
+        const tqfs_params p = m.params[row];
+        long long hs = 0, he = 0, ws, wl;
+        if (m.hist_off != nullptr) {
+            hs = m.hist_off[row];
+            he = m.hist_off[row + 1];
+        }
+        const int mode = row_mode(p, hs, he, m.hist_off != nullptr, m.vocab_total, false, &ws, &wl);
+        int status = TQFS_ROW_OK, token = -1;
+        bool failed = false;
+        for (int r = lane; r < m.nranks; r += 32)
+            failed |= __ldcg(m.recs + (static_cast<size_t>(r) * m.rows + row) * kShardRec + 1) != 0ull;
+        failed = __any_sync(0xFFFFFFFFu, failed);
+        if (mode == kModeGeneral) {
+            status = TQFS_ROW_ERR_UNSUPPORTED;
+        } else if (failed) {
+            status = TQFS_ROW_ERR_TIMEOUT;
+        } else if (mode == kModeGreedy) {
+            unsigned long long t[4] = {0ull, 0ull, 0ull, 0ull};
+            for (int i = lane; i < m.nranks * 4; i += 32)
+                top4_insert(t, __ldcg(m.recs + (static_cast<size_t>(i >> 2) * m.rows + row) * kShardRec + 2 + (i & 3)));
+            unsigned long long o[4];
+            warp_top4(t, o, lane);
+            token = o[0] ? static_cast<int>(key_token(o[0])) : 0;
+        } else {
+            const int k = static_cast<int>(p.top_k);
+            int n = 0;
+            for (int r = 0; r < m.nranks; ++r) {
+                const unsigned long long* rec = m.recs + (static_cast<size_t>(r) * m.rows + row) * kShardRec;
+                const int c = static_cast<int>(min(__ldcg(rec), static_cast<unsigned long long>(kStreamMaxK)));
+                if (n + c > kListCap) warp_keep_top(L, &n, k, bins);
+                for (int i = lane; i < c; i += 32) L[n + i] = __ldcg(rec + 2 + i);
+                n += c;
+                __syncwarp();
+            }
+            token = finish_sampled(p, k, L, n, S, bins, m.uniforms, m.rng_state, row, nullptr);
+        }
+        if (lane == 0) {
+            if (m.out_token != nullptr) m.out_token[row] = token;
+            if (m.out_status != nullptr) m.out_status[row] = status;
+        }
+        __syncwarp();
+    }
 }
 
 template <int DT>
@@ -1078,7 +1175,7 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
     const tqfs_params p = a.params[row];
     const long long hs = a.hist_off[row], he = a.hist_off[row + 1];
     long long ws, wl;
-    if (row_mode(p, hs, he, true, a.vocab, false, &ws, &wl) != kModeStream) return;
+    if (row_mode(p, hs, he, true, a.vocab_route, false, &ws, &wl) != kModeStream) return;
     const int C = a.chunks;
     uint32_t* off = a.win_off + static_cast<size_t>(row) * C * 2;
     if (wl == 0) {
@@ -1095,7 +1192,7 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
 #pragma unroll
     for (int m = 0; m < PER; ++m) {
         const int j = tid + m * NT;
-        tok[m] = j < n ? src[j] : -1;
+        tok[m] = j < n ? src[j] - a.vocab_offset : -1;  // shard-relative id
     }
 #pragma unroll
     for (int m = 0; m < PER; ++m)
@@ -1293,6 +1390,17 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     cfg.attrs = attr;
     cfg.numAttrs = after_window ? 1 : 0;  // overlap its launch with the window kernel
     return cudaLaunchKernelEx(&cfg, kern, a, top4_diag);
+}
+
+cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s) {
+    if (m.rows <= 0) return cudaSuccess;
+    const size_t smem = static_cast<size_t>(kSW) * kMergeSmem;
+    cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const int ctas = (m.rows + kSW - 1) / kSW;
+    merge_kernel<<<ctas, kSW * 32, smem, s>>>(m);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,
