@@ -96,3 +96,40 @@ def test_large_top_k_rows(cuda_device):
     _assert_ok(g)
     rep = compare(b, g)
     assert rep.identical + rep.boundary_ties == rep.rows
+
+
+def test_prefix_sorted_rows_all_branches(cuda_device):
+    """Full-vocabulary rows cut by top_p and/or min_p: the kernel sorts only a
+    prefix of the (p desc, id asc) order (collected by min_p's floor, or by
+    top_p's exponent bins) or falls back to the whole sort when that prefix
+    is too large; every branch must give the oracle's tokens and kept
+    probabilities."""
+    rng = np.random.default_rng(77)
+    V = 151_936
+    cases = [  # (T, top_p, min_p)
+        (0.5, 0.9, None),     # top_p alone, small prefix
+        (1.5, 0.9, None),     # top_p alone, prefix above the shared-memory cap
+        (1.0, 0.6, None),
+        (1.0, 1.0, 0.05),     # min_p alone
+        (1.5, 1.0, 0.001),    # min_p alone, floor prefix above the cap
+        (0.8, 0.3, 0.1),      # top_p cuts before min_p
+        (1.2, 0.95, 0.2),     # min_p cuts before top_p
+        (1.0, 0.0, None),     # top_p 0 keeps one entry
+        (1.0, 0.9, 1.5),      # min_p above 1 keeps one entry
+        (0.2, 0.5, 0.05),     # peaked row
+        (1.0, 0.999, None),
+        (3.0, 0.5, None),     # very flat row
+    ]
+    n = len(cases)
+    x = (3.0 * rng.standard_normal((n, V))).astype(np.float32)
+    for r in range(n):
+        x[r, rng.choice(V, size=2, replace=False)] += 8.0
+    ps = [W.params_rows(1, T, top_p=tp, top_k=0, min_p=mp)[0] for T, tp, mp in cases]
+    for dtype in ("f32", "bf16"):
+        xb = x if dtype == "f32" else W.to_bf16_bits(x)
+        b = _batch(xb, np.array(ps), seed=4, dtype=dtype)
+        g = gpu_sample(b, want_probs=True)
+        _assert_ok(g)
+        rep = compare(b, g)
+        print(dtype, rep)
+        assert rep.identical + rep.boundary_ties == rep.rows

@@ -75,7 +75,486 @@ struct FilterOut {
     int keep;      // kept entries: K[0..keep)
     float total;   // softmax total (mod.rs:180)
     float total2;  // draw total of the kept probabilities (mod.rs:234)
+    int fast;      // 1: filter_row_fast produced it (sums may run as exact_seq_prefix)
 };
+
+}  // namespace tqfs
+
+namespace tqfs {
+
+// ---- the reference's sequential f32 sums, reproduced in parallel -----------
+//
+// s_0 = -0.0, s_{i+1} = fl(s_i + x_i) over nonnegative finite x. While s
+// stays inside one binade e ([2^e, 2^(e+1)), or [0, 2^-125) for e = -126),
+// every partial sum is a multiple of u_e = 2^(e-23), and fl(s + x) =
+// s + rne(x/u_e)*u_e unless x/u_e lies exactly halfway between two integers
+// (the tie then goes by the parity of s). A chunk whose partial sums all stay
+// in binade e therefore adds the integer R_e = sum of rne(x_i/u_e), in any
+// order. The CTA computes R_e for the 3 binades each chunk can start in
+// (taken from an fp64 prefix of the chunk sums, which the sequential sum
+// tracks within (n-1)*2^-24 relative) and one thread walks the chunks: it
+// adds R_e*u_e where the start binade is a candidate, no element was halfway
+// and the end stays below 2^(e+1), and adds the chunk's elements one at a time
+// elsewhere (where the sum changes binade). The walk can stop at the first
+// partial sum that reaches a given value, as the reference's top_p and draw
+// loops do (src/sampling/mod.rs:199-207, 236-245).
+constexpr int kSumChunk = 512;
+constexpr int kSumMaxChunks = 512;  // n <= 262,144
+
+struct SumShared {
+    double d[kSumMaxChunks];  // chunk sums, then the exclusive prefixes
+    unsigned long long r[kSumMaxChunks][3];
+    int elo[kSumMaxChunks];           // the chunk's first candidate binade
+    unsigned char ok[kSumMaxChunks];  // bit q: binade elo + q usable
+    float sum;
+    int at;
+};
+
+// rne(x / 2^(e-23)) for the bits xb of a nonnegative finite x; sets bad when
+// x / 2^(e-23) is halfway between two integers or at least 2^40.
+__device__ __forceinline__ unsigned long long ulps_in_binade(uint32_t xb, int e, bool& bad) {
+    const int ex = static_cast<int>(xb >> 23);
+    const uint32_t mant = ex ? ((xb & 0x7FFFFFu) | 0x800000u) : xb;
+    const int sh = (e - 23) - ((ex ? ex : 1) - 150);  // x / u_e = mant * 2^-sh
+    if (sh <= 0) {
+        if (sh < -16) {
+            bad = true;
+            return 0ull;
+        }
+        return static_cast<unsigned long long>(mant) << (-sh);
+    }
+    if (sh > 25) return 0ull;  // below half a unit
+    const uint32_t rem = mant & ((1u << sh) - 1u), half = 1u << (sh - 1);
+    bad |= rem == half;
+    return static_cast<unsigned long long>((mant >> sh) + (rem > half ? 1u : 0u));
+}
+
+__device__ __forceinline__ int binade_of(double x) {  // floor(log2 x), at least -126
+    if (!(x > 0.0)) return -126;
+    int ex;
+    frexp(x, &ex);
+    return max(ex - 1, -126);
+}
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// The sequential f32 sum s0 + x(0) + x(1) + ... (s0 = -0.0 by default, or a
+// sum this function returned), stopping after the first partial sum >= stop
+// (never, for stop = +inf or NaN) or after n terms (n <= kSumMaxChunks *
+// kSumChunk, every term finite and >= 0). Returns that partial sum to every
+// thread, and in *at how many terms it holds (1-based position of the
+// stopping term, else n).
+template <int NT, class Load>
+__device__ float exact_seq_prefix(Load x, int n, float stop, SumShared* sh, int* at, float s0 = -0.0f) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = NT / 32;
+    const int nch = (n + kSumChunk - 1) / kSumChunk;
+    for (int c = warp; c < nch; c += NW) {
+        const int end = min(n, (c + 1) * kSumChunk);
+        double d = 0.0;
+        for (int i = c * kSumChunk + lane; i < end; i += 32) d += x(i);
+        d = warp_sum_f64(d);
+        if (lane == 0) sh->d[c] = d;
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive prefix of the chunk sums
+        const int per = (nch + 31) / 32;
+        const int b0 = lane * per;
+        double s = 0.0;
+        for (int i = 0; i < per; ++i)
+            if (b0 + i < nch) s += sh->d[b0 + i];
+        double incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        double run = incl - s;
+        for (int i = 0; i < per; ++i) {
+            if (b0 + i < nch) {
+                const double v = sh->d[b0 + i];
+                sh->d[b0 + i] = run;
+                run += v;
+            }
+        }
+    }
+    __syncthreads();
+    for (int c = warp; c < nch; c += NW) {
+        const int e0 = binade_of((static_cast<double>(s0) + sh->d[c]) * (1.0 - 1.0 / 64.0));
+        const int end = min(n, (c + 1) * kSumChunk);
+        unsigned long long r0 = 0ull, r1 = 0ull, r2 = 0ull;
+        bool b0 = false, b1 = false, b2 = false;
+        for (int i = c * kSumChunk + lane; i < end; i += 32) {
+            const uint32_t xb = __float_as_uint(x(i));
+            r0 += ulps_in_binade(xb, e0, b0);
+            r1 += ulps_in_binade(xb, e0 + 1, b1);
+            r2 += ulps_in_binade(xb, e0 + 2, b2);
+        }
+        r0 = warp_sum_u64(r0);
+        r1 = warp_sum_u64(r1);
+        r2 = warp_sum_u64(r2);
+        const unsigned okb = (__any_sync(0xFFFFFFFFu, b0) ? 0u : 1u) |
+                             (__any_sync(0xFFFFFFFFu, b1) ? 0u : 2u) |
+                             (__any_sync(0xFFFFFFFFu, b2) ? 0u : 4u);
+        if (lane == 0) {
+            sh->r[c][0] = r0;
+            sh->r[c][1] = r1;
+            sh->r[c][2] = r2;
+            sh->elo[c] = e0;
+            sh->ok[c] = static_cast<unsigned char>(okb);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float s = s0;
+        int pos = n;
+        bool hit = false;
+        for (int c = 0; c < nch && !hit; ++c) {
+            const int beg = c * kSumChunk, end = min(n, beg + kSumChunk);
+            const uint32_t sb = __float_as_uint(s) & 0x7FFFFFFFu;
+            const int field = static_cast<int>(sb >> 23);
+            const int e = field ? field - 127 : -126;
+            const int q = e - sh->elo[c];
+            if (q >= 0 && q < 3 && ((sh->ok[c] >> q) & 1u)) {
+                const unsigned long long m =
+                    static_cast<unsigned long long>(field ? ((sb & 0x7FFFFFu) | 0x800000u) : sb) + sh->r[c][q];
+                if (m < (1ull << 24)) {
+                    const float t = __double2float_rn(ldexp(static_cast<double>(m), e - 23));  // exact
+                    if (!(t >= stop)) {
+                        s = t;
+                        continue;
+                    }
+                }
+            }
+            int i = beg;
+            for (; i + 8 <= end && !hit; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = x(i + k);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (!hit) {
+                        s = __fadd_rn(s, v[k]);
+                        if (s >= stop) {
+                            pos = i + k + 1;
+                            hit = true;
+                        }
+                    }
+                }
+            }
+            for (; i < end && !hit; ++i) {
+                s = __fadd_rn(s, x(i));
+                if (s >= stop) {
+                    pos = i + 1;
+                    hit = true;
+                }
+            }
+        }
+        sh->sum = s;
+        sh->at = pos;
+    }
+    __syncthreads();
+    *at = sh->at;
+    return sh->sum;
+}
+
+template <int NT>
+__device__ __forceinline__ float exact_seq_sum(const float* x, int n, SumShared* sh) {
+    int at;
+    return exact_seq_prefix<NT>([x](int i) { return x[i]; }, n, INFINITY, sh, &at);
+}
+
+// ---- filter_row over a sorted prefix of the row ----------------------------
+//
+// Rows without a top_k cut whose top_p or min_p cuts the sorted probabilities
+// keep a prefix of the (p desc, id asc) order, so only a prefix that holds
+// the cut needs sorting. The probabilities are binned by their 12 leading
+// bits (exponent and 4 mantissa bits: bins are value ranges, descending bin
+// order is descending p), with each bin's count and exact mass (the integer
+// sum of its significands). The prefix is every bin down to
+//   min_p: the bin of min_p * p_max (every p >= the floor is above it; top_p
+//          either cuts inside it or not before min_p does);
+//   top_p: the first bin where the exact mass M of the bins above, counting c
+//          entries, has M * (1 - c * 2^-23) >= top_p (then the reference's
+//          sequential f32 cumulative, within (c-1) * 2^-24 * M of M, reaches
+//          top_p inside the prefix);
+// the smaller of the two when both apply, else the whole row. The prefix is
+// scattered to K grouped by bin, cut at bin boundaries into segments of at
+// most kSegCap keys, and each segment is sorted in shared memory, so K holds
+// the prefix in order; the top_p cumulative runs segment by segment and stops
+// at the cut.
+constexpr int kBins = 4096;
+constexpr int kSegCap = 16384;      // keys one segment sorts in shared memory
+constexpr int kSegStep = kSegCap / 2;
+constexpr int kMaxSegs = kSumMaxChunks * kSumChunk / kSegStep + 1;
+
+struct FastShared {
+    SumShared sum;
+    unsigned long long mant[kBins];  // per bin: sum of 24-bit significands
+    unsigned int cnt[kBins];         // per bin: entries, then the next write position in K
+    int bnd[kMaxSegs + 1];           // segment j starts at bnd[j]
+    int lo_bin, lo_min, m, nseg, fail;
+};
+
+// Dynamic shared memory of a kernel that passes fs and sk to filter_row: a
+// FastShared, then kSegCap keys.
+constexpr int kFastSharedBytes = static_cast<int>((sizeof(FastShared) + 15) / 16 * 16);
+constexpr int kFilterSmemBytes = kFastSharedBytes + kSegCap * 8;
+
+// Descending bitonic sort of n2 (a power of two) keys in shared memory.
+template <int NT>
+__device__ __forceinline__ void bitonic_desc_smem(unsigned long long* keys, int n2) {
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < (n2 >> 1); i += NT) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool desc = (lo & size) == 0;
+                const unsigned long long a = keys[lo], b = keys[hi];
+                if ((a < b) == desc) {
+                    keys[lo] = b;
+                    keys[hi] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t sig24(uint32_t pb) {  // p = sig24 * 2^(max(ex,1) - 150)
+    return (pb >> 23) ? ((pb & 0x7FFFFFu) | 0x800000u) : pb;
+}
+
+__device__ __forceinline__ double bin_mass(unsigned long long mant, int bin) {
+    const int ex = bin >> 4;
+    return ldexp(static_cast<double>(mant), (ex ? ex : 1) - 150);
+}
+
+// filter_row's result for a qualifying row (see above). Returns false, having
+// changed nothing but E and K, when the row does not qualify: a top_k cut,
+// neither top_p nor min_p, more than kSumMaxChunks * kSumChunk ids, a
+// non-finite exponential, a segment above kSegCap, or a top_p prefix whose
+// cumulative does not reach top_p.
+template <int NT = kFilterThreads>
+__device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K, int V,
+                                const tqfs_params& p, float* red, FilterOut* out, FastShared* fs,
+                                unsigned long long* sk) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t k = p.top_k;
+    if (k != 0u && k < static_cast<uint32_t>(V)) return false;
+    const bool top_p_on = !(p.top_p >= 1.0f);
+    const bool min_p_on = (p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f);
+    if ((!top_p_on && !min_p_on) || V > kSumMaxChunks * kSumChunk) return false;
+    // ---- softmax (mod.rs:166-190) -----------------------------------------
+    float lmax = -INFINITY;
+    for (int j = tid; j < V; j += NT) lmax = fmaxf(lmax, W[j]);
+    const float mx = block_max(lmax, red);
+    bool bad = false;
+    for (int j = tid; j < V; j += NT) {
+        const float e = exp_f32(__fdiv_rn(__fsub_rn(W[j], mx), p.temperature));
+        E[j] = e;
+        bad |= !isfinite(e);
+    }
+    if (__syncthreads_or(bad)) return false;
+    const float total = exact_seq_sum<NT>(E, V, &fs->sum);
+    // the largest exponential is exp(0) = 1, so p_max = 1 / total
+    const float pmax = total > 0.0f ? __fdiv_rn(1.0f, total) : 1.0f;
+    // ---- bins: counts and exact masses ------------------------------------
+    for (int i = tid; i < kBins; i += NT) {
+        fs->cnt[i] = 0u;
+        fs->mant[i] = 0ull;
+    }
+    __syncthreads();
+    for (int j0 = 0; j0 < V; j0 += NT) {
+        const int j = j0 + tid;
+        const bool in = j < V;
+        uint32_t pb = 0u;
+        if (in) pb = __float_as_uint(total > 0.0f ? __fdiv_rn(E[j], total) : E[j]);
+        const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
+        if (in) {
+            const uint32_t bin = pb >> 19;
+            const unsigned peers = __match_any_sync(act, bin);
+            const unsigned msum = __reduce_add_sync(peers, sig24(pb));
+            if (lane == __ffs(peers) - 1) {
+                atomicAdd(&fs->cnt[bin], static_cast<unsigned>(__popc(peers)));
+                atomicAdd(&fs->mant[bin], static_cast<unsigned long long>(msum));
+            }
+        }
+    }
+    __syncthreads();
+    // ---- the prefix's lowest bin, positions and segments (warp 0) ---------
+    if (warp == 0) {
+        constexpr int kPer = kBins / 32;  // lane l: bins kBins-1-kPer*l downwards
+        const int top = kBins - 1 - kPer * lane;
+        int lo_min = -1;
+        if (min_p_on) {
+            const float fl = fminf(__fmul_rn(p.min_p, pmax), pmax);  // NaN: p_max
+            lo_min = static_cast<int>(__float_as_uint(fl) >> 19);
+        }
+        int lo_top = -1;
+        if (top_p_on) {
+            double ml = 0.0;
+            unsigned cl = 0u;
+            for (int i = 0; i < kPer; ++i) {
+                ml += bin_mass(fs->mant[top - i], top - i);
+                cl += fs->cnt[top - i];
+            }
+            double mi = ml;
+            unsigned ci = cl;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double y = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+                const unsigned z = __shfl_up_sync(0xFFFFFFFFu, ci, o);
+                if (lane >= o) {
+                    mi += y;
+                    ci += z;
+                }
+            }
+            double mm = mi - ml;
+            unsigned cc = ci - cl;
+            int found = -1;
+            for (int i = 0; i < kPer && found < 0; ++i) {
+                const unsigned c = fs->cnt[top - i];
+                mm += bin_mass(fs->mant[top - i], top - i);
+                cc += c;
+                if (c != 0u && mm * (1.0 - ldexp(static_cast<double>(cc), -23)) >= static_cast<double>(p.top_p))
+                    found = top - i;
+            }
+            const unsigned bal = __ballot_sync(0xFFFFFFFFu, found >= 0);
+            if (bal) lo_top = __shfl_sync(0xFFFFFFFFu, found, __ffs(bal) - 1);
+        }
+        int lo = 0;
+        if (min_p_on) lo = max(lo_min, lo_top);
+        else if (lo_top >= 0) lo = lo_top;
+        // positions in K: descending bins from lo
+        unsigned cl = 0u;
+        for (int i = 0; i < kPer; ++i)
+            if (top - i >= lo) cl += fs->cnt[top - i];
+        unsigned ci = cl;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned z = __shfl_up_sync(0xFFFFFFFFu, ci, o);
+            if (lane >= o) ci += z;
+        }
+        const int m = static_cast<int>(__shfl_sync(0xFFFFFFFFu, ci, 31));
+        const int nseg = (m + kSegStep - 1) / kSegStep;
+        unsigned pos = ci - cl;
+        for (int i = 0; i < kPer; ++i) {
+            const int b = top - i;
+            if (b < lo) break;
+            const unsigned c = fs->cnt[b];
+            fs->cnt[b] = pos;  // write cursor
+            if (c != 0u) {  // segment j >= 1 starts at the bin holding position j * kSegStep
+                for (int j = static_cast<int>((pos + kSegStep - 1) / kSegStep); j * kSegStep < static_cast<int>(pos + c); ++j)
+                    if (j >= 1) fs->bnd[j] = static_cast<int>(pos);
+            }
+            pos += c;
+        }
+        if (lane == 0) {
+            fs->lo_bin = lo;
+            fs->lo_min = lo_min;
+            fs->m = m;
+            fs->nseg = nseg;
+            fs->bnd[0] = 0;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            int fail = 0;
+            for (int j = 0; j < nseg; ++j) {
+                const int hi = j + 1 < nseg ? fs->bnd[j + 1] : m;
+                fail |= hi - fs->bnd[j] > kSegCap;
+            }
+            fs->fail = fail;
+        }
+    }
+    __syncthreads();
+    if (fs->fail) return false;
+    const int lo_bin = fs->lo_bin, m = fs->m, nseg = fs->nseg;
+    // ---- scatter the prefix to K, grouped by bin --------------------------
+    for (int j0 = 0; j0 < V; j0 += NT) {
+        const int j = j0 + tid;
+        float pj = 0.0f;
+        bool take = false;
+        uint32_t bin = 0u;
+        if (j < V) {
+            pj = total > 0.0f ? __fdiv_rn(E[j], total) : E[j];
+            bin = __float_as_uint(pj) >> 19;
+            take = static_cast<int>(bin) >= lo_bin;
+        }
+        const unsigned act = __ballot_sync(0xFFFFFFFFu, take);
+        if (take) {
+            const unsigned peers = __match_any_sync(act, bin);
+            const int leader = __ffs(peers) - 1;
+            unsigned base = 0u;
+            if (lane == leader) base = atomicAdd(&fs->cnt[bin], static_cast<unsigned>(__popc(peers)));
+            base = __shfl_sync(peers, base, leader);
+            K[base + __popc(peers & ((1u << lane) - 1u))] = make_key(order32(pj), static_cast<uint32_t>(j));
+        }
+    }
+    __syncthreads();
+    // ---- sort segment by segment; top_p (mod.rs:195-209) ------------------
+    float cum = -0.0f;
+    int n_top = -1;  // the top_p cut (terms), once reached
+    for (int j = 0; j < nseg && n_top < 0; ++j) {
+        const int s0 = fs->bnd[j];
+        const int s1 = j + 1 < nseg ? fs->bnd[j + 1] : m;
+        const int n = s1 - s0;
+        if (n <= 0) continue;
+        const int n2 = pow2_at_least(n);
+        for (int i = tid; i < n2; i += NT) sk[i] = i < n ? K[s0 + i] : 0ull;
+        __syncthreads();
+        bitonic_desc_smem<NT>(sk, n2);
+        for (int i = tid; i < n; i += NT) K[s0 + i] = sk[i];
+        if (top_p_on) {
+            int at;
+            cum = exact_seq_prefix<NT>([sk](int i) { return key_value(sk[i]); }, n, p.top_p, &fs->sum, &at, cum);
+            if (cum >= p.top_p) n_top = s0 + at;
+        }
+        __syncthreads();
+    }
+    // top_p not reached: conclusive only when the prefix is the whole row or
+    // min_p's (top_p then keeps more than min_p does)
+    if (top_p_on && n_top < 0 && lo_bin != 0 && !(min_p_on && lo_bin == fs->lo_min)) return false;
+    // ---- min_p (mod.rs:213-224) and the draw total ------------------------
+    auto val = [K](int i) { return key_value(K[i]); };
+    int keep = n_top >= 0 ? n_top : m;
+    if (min_p_on) {
+        const float f2 = __fmul_rn(p.min_p, key_value(K[0]));
+        int cnt = 0;
+        for (int i0 = 0; i0 < keep; i0 += NT) {
+            const int i = i0 + tid;
+            cnt += __syncthreads_count(i < keep && key_value(K[i]) >= f2);
+        }
+        keep = cnt < 1 ? 1 : cnt;
+    }
+    float total2 = cum;
+    if (!(n_top >= 0 && keep == n_top)) {
+        int at;
+        total2 = exact_seq_prefix<NT>(val, keep, INFINITY, &fs->sum, &at);
+    }
+    if (tid == 0) {
+        out->keep = keep;
+        out->total = total;
+        out->total2 = total2;
+        out->fast = 1;
+    }
+    __syncthreads();
+    return true;
+}
+
+}  // namespace tqfs
+
+namespace tqfs {
 
 // W[0..V) holds the row's (penalised) logits. Leaves in K[0..keep) the kept
 // candidates as probability keys (order32(p) << 32 | ~token), sorted as the
@@ -88,11 +567,16 @@ struct FilterOut {
 //     sequential f32 total from -0.0, division when total > 0, sort;
 //   apply_top_p (mod.rs:195-209) and apply_min_p (mod.rs:213-224);
 //   the draw total (mod.rs:234).
-// W is reused for the candidates' tokens; E holds the exponentials; K needs
-// pow2_at_least(V) entries.
+// With fs (and sk, kSegCap keys of shared memory) rows that qualify take
+// filter_row_fast, and the sequential sums of finite rows run as
+// exact_seq_prefix; without, every sum is one thread's loop. W is reused for
+// the candidates' tokens; E holds the exponentials; K needs pow2_at_least(V)
+// entries.
 template <int NT = kFilterThreads>
 __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
-                           const tqfs_params& p, float* red, FilterOut* out) {
+                           const tqfs_params& p, float* red, FilterOut* out,
+                           FastShared* fs = nullptr, unsigned long long* sk = nullptr) {
+    if (fs != nullptr && filter_row_fast<NT>(W, E, K, V, p, red, out, fs, sk)) return;
     const int tid = threadIdx.x;
     const uint32_t k = p.top_k;
     const bool topk = k != 0u && k < static_cast<uint32_t>(V);
@@ -110,26 +594,36 @@ __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
         lmax = fmaxf(lmax, v);  // NaN never wins, as f32::max
     }
     const float mx = block_max(lmax, red);
+    bool bad = false;
     for (int j = tid; j < nc; j += NT) {
         const float v = topk ? key_value(K[j]) : W[j];
-        E[j] = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
+        const float e = exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature));
+        E[j] = e;
+        bad |= !isfinite(e);
     }
-    __syncthreads();
-    if (tid == 0) {
-        float total = -0.0f;
-        int j = 0;
-        for (; j + 8 <= nc; j += 8) {
-            float x[8];
+    const bool any_bad = __syncthreads_or(bad) != 0;
+    // every probability is finite and >= 0 when every exponential is
+    const bool exact = fs != nullptr && !any_bad && nc <= kSumMaxChunks * kSumChunk;
+    float total;
+    if (exact) {
+        total = exact_seq_sum<NT>(E, nc, &fs->sum);
+    } else {
+        if (tid == 0) {
+            float t = -0.0f;
+            int j = 0;
+            for (; j + 8 <= nc; j += 8) {
+                float x[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) x[q] = E[j + q];
+                for (int q = 0; q < 8; ++q) x[q] = E[j + q];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) total = __fadd_rn(total, x[q]);
+                for (int q = 0; q < 8; ++q) t = __fadd_rn(t, x[q]);
+            }
+            for (; j < nc; ++j) t = __fadd_rn(t, E[j]);
+            out->total = t;
         }
-        for (; j < nc; ++j) total = __fadd_rn(total, E[j]);
-        out->total = total;
+        __syncthreads();
+        total = out->total;
     }
-    __syncthreads();
-    const float total = out->total;
     const int n2 = pow2_at_least(nc);
     // Candidate tokens go to W (dead once E is computed) so that K can be
     // rewritten with probability keys.
@@ -147,9 +641,39 @@ __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
     }
     __syncthreads();
     bitonic_desc(K, n2);
+    const bool top_p_on = !(p.top_p >= 1.0f);
+    const bool min_p_on = (p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f);
+    if (exact) {
+        auto val = [K](int i) { return key_value(K[i]); };
+        int keep = nc, at = nc;
+        float cum = 0.0f;
+        if (top_p_on) {
+            cum = exact_seq_prefix<NT>(val, nc, p.top_p, &fs->sum, &at);
+            keep = at;  // the terms taken: at least 1
+        }
+        if (min_p_on) {
+            const float floor = __fmul_rn(p.min_p, key_value(K[0]));
+            int cnt = 0;
+            for (int i0 = 0; i0 < keep; i0 += NT) {
+                const int i = i0 + tid;
+                cnt += __syncthreads_count(i < keep && key_value(K[i]) >= floor);
+            }
+            keep = cnt < 1 ? 1 : cnt;
+        }
+        float total2 = cum;
+        if (!(top_p_on && keep == at)) total2 = exact_seq_prefix<NT>(val, keep, INFINITY, &fs->sum, &at);
+        if (tid == 0) {
+            out->keep = keep;
+            out->total = total;
+            out->total2 = total2;
+            out->fast = 0;
+        }
+        __syncthreads();
+        return;
+    }
     if (tid == 0) {
         int keep = nc;
-        if (!(p.top_p >= 1.0f)) {
+        if (top_p_on) {
             float cum = 0.0f;
             int n = 0;
             for (int i = 0; i < nc; ++i) {
@@ -160,7 +684,7 @@ __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
             keep = n < 1 ? 1 : n;
             if (keep > nc) keep = nc;
         }
-        if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
+        if (min_p_on && keep > 0) {
             const float floor = __fmul_rn(p.min_p, key_value(K[0]));
             int n = 0;
             while (n < keep && key_value(K[n]) >= floor) ++n;
@@ -169,7 +693,9 @@ __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
         float total2 = -0.0f;
         for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, key_value(K[i]));
         out->keep = keep;
+        out->total = total;
         out->total2 = total2;
+        out->fast = 0;
     }
     __syncthreads();
 }
@@ -188,6 +714,27 @@ __device__ __forceinline__ int draw_kept(const unsigned long long* K, int keep, 
         if (cum >= target) return static_cast<int>(key_token(K[i]));
     }
     return static_cast<int>(key_token(K[keep - 1]));
+}
+
+// The draw (mod.rs:227-248) over a filter_row result with uniform u: the
+// first kept entry when the total is not a positive number, else the first
+// entry whose sequential cumulative reaches u * total2. Returns the token to
+// every thread.
+template <int NT = kFilterThreads>
+__device__ int draw_row(const unsigned long long* K, const FilterOut& fo, float u, FastShared* fs,
+                        int* shared_word) {
+    const int keep = fo.keep;
+    if (fo.fast && keep > 0 && isfinite(fo.total2) && fo.total2 > 0.0f) {
+        int at;
+        exact_seq_prefix<NT>([K](int i) { return key_value(K[i]); }, keep, __fmul_rn(u, fo.total2),
+                             &fs->sum, &at);
+        return static_cast<int>(key_token(K[at - 1]));
+    }
+    if (threadIdx.x == 0) *shared_word = draw_kept(K, keep, fo.total2, u);
+    __syncthreads();
+    const int t = *shared_word;
+    __syncthreads();
+    return t;
 }
 
 }  // namespace tqfs

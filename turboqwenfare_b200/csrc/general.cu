@@ -1,21 +1,23 @@
 // General kernel: the sampled rows the stream kernel does not own (top_k
 // None/0, top_k >= vocab, top_k > kStreamMaxK, or a penalty window longer
-// than kWinCap). These rows run the reference's
-// full filter chain over up to the whole vocabulary, and its result depends
-// on the f32 rounding of three sequential sums the reference performs
-// (src/sampling/mod.rs:180, 199-207, 234-245): over ~150k terms those sums
-// drop every addend below half an ulp of the running total, so a more
-// accurate summation would produce different tokens. This kernel reproduces
-// the reference's arithmetic exactly:
+// than kWinCap). These rows run the reference's full filter chain over up to
+// the whole vocabulary, and its result depends on the f32 rounding of three
+// sequential sums the reference performs (src/sampling/mod.rs:180, 199-207,
+// 234-245): over ~150k terms those sums drop every addend below half an ulp
+// of the running total, so a more accurate summation would produce different
+// tokens. This kernel reproduces the reference's arithmetic exactly
+// (filter.cuh):
 //   - candidates in the reference's order (token order without top_k; the
 //     pinned (value desc, id asc) order after top_k);
-//   - max, exp((v - max) / T), the sequential f32 total, p = e / total;
-//   - the (p desc, id asc) order by a bitonic sort of 64-bit order keys;
-//   - top_p, min_p and the inverse-CDF draw with the sequential f32
-//     cumulative sums, done by one thread in order.
+//   - max, exp((v - max) / T), the sequential f32 total, p = e / total, all
+//     sums by the exact parallel emulation of the sequential f32 sum;
+//   - rows cut by top_p or min_p sort only a prefix of the (p desc, id asc)
+//     order that holds the cut, in shared memory; other rows sort 64-bit
+//     order keys of the whole candidate list;
+//   - top_p, min_p and the inverse-CDF draw over that order.
 // One CTA per row (persistent over the general rows), working arrays in
-// library scratch. Correctness first: the sequential sums run at one add
-// per few cycles per row.
+// library scratch, the prefix sort and the sums' chunk tables in dynamic
+// shared memory.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -44,6 +46,10 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
     __shared__ float red[kGenThreads / 32];
     __shared__ int sh_int[4];
     __shared__ FilterOut fo;
+    __shared__ float sh_u;
+    extern __shared__ __align__(16) unsigned char dyn_smem[];
+    FastShared* fs = reinterpret_cast<FastShared*>(dyn_smem);
+    unsigned long long* sk = reinterpret_cast<unsigned long long*>(dyn_smem + kFastSharedBytes);
     const int tid = threadIdx.x;
     const int V = a.vocab;
     float* W = g.work + static_cast<size_t>(blockIdx.x) * g.stride;
@@ -99,32 +105,26 @@ __global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, Gene
             __syncthreads();
         }
         // ---- top_k, softmax, top_p, min_p (mod.rs:153-224) ---------------
-        filter_row(W, E, K, V, p, red, &fo);
+        filter_row(W, E, K, V, p, red, &fo, fs, sk);
         // ---- draw (mod.rs:227-248) ----------------------------------------
+        const int keep = fo.keep;
         if (tid == 0) {
-            const int keep = fo.keep;
-            int tok = 0;
-            if (keep > 0) {
-                float u = 0.0f;
-                if (isfinite(fo.total2) && fo.total2 > 0.0f) {  // a uniform is consumed
-                    if (a.uniforms != nullptr) {
-                        u = a.uniforms[row];
-                    } else {
-                        uint64_t s4[4];
-                        uint64_t* st = a.rng_state + static_cast<size_t>(row) * 4;
-                        for (int q = 0; q < 4; ++q) s4[q] = st[q];
-                        u = xoshiro_next_f32(s4);
-                        for (int q = 0; q < 4; ++q) st[q] = s4[q];
-                    }
+            float u = 0.0f;
+            if (keep > 0 && isfinite(fo.total2) && fo.total2 > 0.0f) {  // a uniform is consumed
+                if (a.uniforms != nullptr) {
+                    u = a.uniforms[row];
+                } else {
+                    uint64_t s4[4];
+                    uint64_t* st = a.rng_state + static_cast<size_t>(row) * 4;
+                    for (int q = 0; q < 4; ++q) s4[q] = st[q];
+                    u = xoshiro_next_f32(s4);
+                    for (int q = 0; q < 4; ++q) st[q] = s4[q];
                 }
-                tok = draw_kept(K, keep, fo.total2, u);
             }
-            sh_int[0] = tok;
-            sh_int[1] = keep;
+            sh_u = u;
         }
         __syncthreads();
-        const int token = sh_int[0];
-        const int keep = sh_int[1];
+        const int token = keep > 0 ? draw_row<kGenThreads>(K, fo, sh_u, fs, &sh_int[0]) : 0;
         if (a.out_probs != nullptr) {
             float* pr = a.out_probs + base;
             for (int i = tid; i < V; i += kGenThreads) pr[i] = 0.0f;
@@ -154,8 +154,20 @@ size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_st
 
 cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s) {
     if (a.rows <= 0 || a.vocab <= 0 || ctas <= 0) return cudaSuccess;
-    if (a.dtype == TQFS_DTYPE_F32) general_kernel<0><<<ctas, kGenThreads, 0, s>>>(a, g);
-    else general_kernel<1><<<ctas, kGenThreads, 0, s>>>(a, g);
+    const int smem = kFilterSmemBytes;
+    static thread_local int configured = -1;  // the device whose attributes are set
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (configured != dev) {
+        e = cudaFuncSetAttribute(general_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(general_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured = dev;
+    }
+    if (a.dtype == TQFS_DTYPE_F32) general_kernel<0><<<ctas, kGenThreads, smem, s>>>(a, g);
+    else general_kernel<1><<<ctas, kGenThreads, smem, s>>>(a, g);
     return cudaGetLastError();
 }
 

@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kMT) mtp_kernel(MtpArgs m, MtpScratch g) {
     __shared__ FilterOut ft, fd;
     __shared__ float qv[2];
     __shared__ int sh[4];
+    extern __shared__ __align__(16) unsigned char dyn_smem[];
+    FastShared* fs = reinterpret_cast<FastShared*>(dyn_smem);
+    unsigned long long* sk = reinterpret_cast<unsigned long long*>(dyn_smem + kFastSharedBytes);
     const int tid = threadIdx.x;
     const Workspace A = workspace(g, blockIdx.x, 0);
     const Workspace B = workspace(g, blockIdx.x, 1);
@@ -179,9 +182,9 @@ __global__ void __launch_bounds__(kMT) mtp_kernel(MtpArgs m, MtpScratch g) {
                 }
             } else {
                 load_row<DT>(m, m.target, trow0 + j, A.W);
-                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft);
+                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft, fs, sk);
                 load_row<DT>(m, m.draft, drow0 + j, B.W);
-                filter_row(B.W, B.E, B.K, m.vocab, p, red, &fd);
+                filter_row(B.W, B.E, B.K, m.vocab, p, red, &fd, fs, sk);
                 q_of(A, ft, x, m.vocab, &qv[0]);
                 q_of(B, fd, x, m.vocab, &qv[1]);
                 ok = __fmul_rn(us[j], qv[1]) < qv[0];
@@ -207,11 +210,8 @@ __global__ void __launch_bounds__(kMT) mtp_kernel(MtpArgs m, MtpScratch g) {
                 token = row_argmax<DT>(m, m.target, trow0 + L, redk);
             } else {
                 load_row<DT>(m, m.target, trow0 + L, A.W);
-                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft);
-                if (tid == 0) sh[0] = draw_kept(A.K, ft.keep, ft.total2, us[L]);
-                __syncthreads();
-                token = sh[0];
-                __syncthreads();
+                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft, fs, sk);
+                token = draw_row<kMT>(A.K, ft, us[L], fs, &sh[0]);
             }
         }
         if (tid == 0) {
@@ -237,8 +237,19 @@ size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride
 
 cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s) {
     if (m.seqs <= 0 || ctas <= 0) return cudaSuccess;
-    if (m.dtype == TQFS_DTYPE_F32) mtp_kernel<0><<<ctas, kMT, 0, s>>>(m, g);
-    else mtp_kernel<1><<<ctas, kMT, 0, s>>>(m, g);
+    const int smem = kFilterSmemBytes;
+    static thread_local int configured = -1;  // the device whose attributes are set
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (configured != dev) {
+        e = cudaFuncSetAttribute(mtp_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mtp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured = dev;
+    }
+    if (m.dtype == TQFS_DTYPE_F32) mtp_kernel<0><<<ctas, kMT, smem, s>>>(m, g);
+    else mtp_kernel<1><<<ctas, kMT, smem, s>>>(m, g);
     return cudaGetLastError();
 }
 
