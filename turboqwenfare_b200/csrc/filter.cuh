@@ -90,22 +90,24 @@ namespace tqfs {
 // s + rne(x/u_e)*u_e unless x/u_e lies exactly halfway between two integers
 // (the tie then goes by the parity of s). A chunk whose partial sums all stay
 // in binade e therefore adds the integer R_e = sum of rne(x_i/u_e), in any
-// order. The CTA computes R_e for the 3 binades each chunk can start in
+// order. The CTA computes R_e for the 2 binades each chunk can start in
 // (taken from an fp64 prefix of the chunk sums, which the sequential sum
-// tracks within (n-1)*2^-24 relative) and one thread walks the chunks: it
-// adds R_e*u_e where the start binade is a candidate, no element was halfway
-// and the end stays below 2^(e+1), and adds the chunk's elements one at a time
-// elsewhere (where the sum changes binade). The walk can stop at the first
+// tracks within (n-1)*2^-24 relative) and one warp walks the chunks: it adds
+// R_e*u_e where the start binade is a candidate, no element was halfway and
+// the end stays below 2^(e+1); elsewhere (where the sum changes binade) it
+// repeats the same by groups of 32 terms, and term by term inside a group
+// that still does not qualify (walk_group). The walk can stop at the first
 // partial sum that reaches a given value, as the reference's top_p and draw
 // loops do (src/sampling/mod.rs:199-207, 236-245).
 constexpr int kSumChunk = 512;
+constexpr int kBatch = 8;  // loads a thread keeps in flight in a pass over a row
 constexpr int kSumMaxChunks = 512;  // n <= 262,144
 
 struct SumShared {
     double d[kSumMaxChunks];  // chunk sums, then the exclusive prefixes
-    unsigned long long r[kSumMaxChunks][3];
+    unsigned long long r[kSumMaxChunks][2];
     int elo[kSumMaxChunks];           // the chunk's first candidate binade
-    unsigned char ok[kSumMaxChunks];  // bit q: binade elo + q usable
+    unsigned char ok[kSumMaxChunks];  // bit q: binade elo + q usable (q < 2)
     float sum;
     int at;
 };
@@ -148,6 +150,54 @@ __device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v)
     return v;
 }
 
+// Adds the group's terms (lane j holds term g0 + j, j < gn) to s in order,
+// as the warp: each round takes the terms' units in the binade of s
+// (ulps_in_binade) and their inclusive prefix; the terms before the first
+// that is halfway, leaves the binade or reaches stop are added as integers,
+// that one by the f32 add itself, and the round repeats from the next term.
+// Stops (hit, pos = 1-based position) at the first partial sum >= stop.
+__device__ __forceinline__ void walk_group(float v, int g0, int gn, float& s, float stop, int& pos,
+                                           bool& hit) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t vb = __float_as_uint(v);
+    int k0 = 0;
+    while (k0 < gn) {
+        // s >= 0 in binade e: adding n units of 2^(e-23) adds n to its bits
+        // while the result stays below 2^(e+1)
+        const uint32_t sb = __float_as_uint(s) & 0x7FFFFFFFu;
+        const uint32_t bi = max(sb >> 23, 1u);  // biased binade (e + 127)
+        const bool act = lane >= k0 && lane < gn;
+        bool bad = false;
+        unsigned long long r = 0ull;
+        if (act) r = ulps_in_binade(vb, static_cast<int>(bi) - 127, bad);
+        unsigned long long pre = r;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long y = __shfl_up_sync(0xFFFFFFFFu, pre, o);
+            if (lane >= o) pre += y;
+        }
+        const unsigned long long nb = sb + pre;
+        const bool over = nb >= (static_cast<unsigned long long>(bi + 1u) << 23);
+        const float t = __uint_as_float(static_cast<uint32_t>(nb));
+        const unsigned evm = __ballot_sync(0xFFFFFFFFu, act && (bad || over || t >= stop));
+        if (evm == 0u) {
+            s = __shfl_sync(0xFFFFFFFFu, t, gn - 1);
+            return;
+        }
+        const int k = __ffs(evm) - 1;
+        const float before = __shfl_sync(0xFFFFFFFFu, t, k > 0 ? k - 1 : 0);
+        const float xk = __shfl_sync(0xFFFFFFFFu, v, k);
+        if (k > k0) s = before;
+        s = __fadd_rn(s, xk);
+        if (s >= stop) {
+            pos = g0 + k + 1;
+            hit = true;
+            return;
+        }
+        k0 = k + 1;
+    }
+}
+
 // The sequential f32 sum s0 + x(0) + x(1) + ... (s0 = -0.0 by default, or a
 // sum this function returned), stopping after the first partial sum >= stop
 // (never, for stop = +inf or NaN) or after n terms (n <= kSumMaxChunks *
@@ -161,8 +211,15 @@ __device__ float exact_seq_prefix(Load x, int n, float stop, SumShared* sh, int*
     const int nch = (n + kSumChunk - 1) / kSumChunk;
     for (int c = warp; c < nch; c += NW) {
         const int end = min(n, (c + 1) * kSumChunk);
+        float v[kSumChunk / 32];
+#pragma unroll
+        for (int g = 0; g < kSumChunk / 32; ++g) {
+            const int i = c * kSumChunk + g * 32 + lane;
+            v[g] = i < end ? x(i) : 0.0f;
+        }
         double d = 0.0;
-        for (int i = c * kSumChunk + lane; i < end; i += 32) d += x(i);
+#pragma unroll
+        for (int g = 0; g < kSumChunk / 32; ++g) d += v[g];
         d = warp_sum_f64(d);
         if (lane == 0) sh->d[c] = d;
     }
@@ -192,76 +249,103 @@ __device__ float exact_seq_prefix(Load x, int n, float stop, SumShared* sh, int*
     for (int c = warp; c < nch; c += NW) {
         const int e0 = binade_of((static_cast<double>(s0) + sh->d[c]) * (1.0 - 1.0 / 64.0));
         const int end = min(n, (c + 1) * kSumChunk);
-        unsigned long long r0 = 0ull, r1 = 0ull, r2 = 0ull;
-        bool b0 = false, b1 = false, b2 = false;
-        for (int i = c * kSumChunk + lane; i < end; i += 32) {
-            const uint32_t xb = __float_as_uint(x(i));
+        unsigned long long r0 = 0ull, r1 = 0ull;
+        bool b0 = false, b1 = false;
+        float v[kSumChunk / 32];
+#pragma unroll
+        for (int g = 0; g < kSumChunk / 32; ++g) {
+            const int i = c * kSumChunk + g * 32 + lane;
+            v[g] = i < end ? x(i) : 0.0f;  // a zero term adds nothing
+        }
+#pragma unroll
+        for (int g = 0; g < kSumChunk / 32; ++g) {
+            const uint32_t xb = __float_as_uint(v[g]);
             r0 += ulps_in_binade(xb, e0, b0);
             r1 += ulps_in_binade(xb, e0 + 1, b1);
-            r2 += ulps_in_binade(xb, e0 + 2, b2);
         }
         r0 = warp_sum_u64(r0);
         r1 = warp_sum_u64(r1);
-        r2 = warp_sum_u64(r2);
-        const unsigned okb = (__any_sync(0xFFFFFFFFu, b0) ? 0u : 1u) |
-                             (__any_sync(0xFFFFFFFFu, b1) ? 0u : 2u) |
-                             (__any_sync(0xFFFFFFFFu, b2) ? 0u : 4u);
+        const unsigned okb = (__any_sync(0xFFFFFFFFu, b0) ? 0u : 1u) | (__any_sync(0xFFFFFFFFu, b1) ? 0u : 2u);
         if (lane == 0) {
             sh->r[c][0] = r0;
             sh->r[c][1] = r1;
-            sh->r[c][2] = r2;
             sh->elo[c] = e0;
             sh->ok[c] = static_cast<unsigned char>(okb);
         }
     }
     __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {  // the walk; every lane holds the same s
         float s = s0;
         int pos = n;
         bool hit = false;
         for (int c = 0; c < nch && !hit; ++c) {
             const int beg = c * kSumChunk, end = min(n, beg + kSumChunk);
+            const unsigned long long ra = sh->r[c][0], rb = sh->r[c][1];
+            const int elo = sh->elo[c];
+            const unsigned okc = sh->ok[c];
+            // s >= 0 in binade e: adding n units of 2^(e-23) adds n to its
+            // bits while the result stays below 2^(e+1)
             const uint32_t sb = __float_as_uint(s) & 0x7FFFFFFFu;
-            const int field = static_cast<int>(sb >> 23);
-            const int e = field ? field - 127 : -126;
-            const int q = e - sh->elo[c];
-            if (q >= 0 && q < 3 && ((sh->ok[c] >> q) & 1u)) {
-                const unsigned long long m =
-                    static_cast<unsigned long long>(field ? ((sb & 0x7FFFFFu) | 0x800000u) : sb) + sh->r[c][q];
-                if (m < (1ull << 24)) {
-                    const float t = __double2float_rn(ldexp(static_cast<double>(m), e - 23));  // exact
+            const uint32_t bi = max(sb >> 23, 1u);  // biased binade (e + 127)
+            const int e = static_cast<int>(bi) - 127;
+            const int q = e - elo;
+            if (q >= 0 && q < 2 && ((okc >> q) & 1u)) {
+                const unsigned long long nb = sb + (q ? rb : ra);
+                if (nb < (static_cast<unsigned long long>(bi + 1u) << 23)) {
+                    const float t = __uint_as_float(static_cast<uint32_t>(nb));
                     if (!(t >= stop)) {
                         s = t;
                         continue;
                     }
                 }
             }
-            int i = beg;
-            for (; i + 8 <= end && !hit; i += 8) {
-                float v[8];
+            // the chunk by groups of 32 terms: each group's units in the
+            // binades e and e + 1 (below 2^26 a term, else the group is
+            // walked), added whole where its partial sums stay in the binade,
+            // else term by term (walk_group)
+            float v[kSumChunk / 32];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = x(i + k);
+            for (int g = 0; g < kSumChunk / 32; ++g) {
+                const int i = beg + g * 32 + lane;
+                v[g] = i < end ? x(i) : 0.0f;
+            }
+            unsigned gr[kSumChunk / 32][2];
+            unsigned gok = 0u;  // bit 2g + q: group g usable in binade e + q
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    if (!hit) {
-                        s = __fadd_rn(s, v[k]);
-                        if (s >= stop) {
-                            pos = i + k + 1;
-                            hit = true;
+            for (int g = 0; g < kSumChunk / 32; ++g) {
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    bool bad = false;
+                    const unsigned long long u = ulps_in_binade(__float_as_uint(v[g]), e + qq, bad);
+                    bad |= u >= (1ull << 26);
+                    gr[g][qq] = __reduce_add_sync(0xFFFFFFFFu, bad ? 0u : static_cast<unsigned>(u));
+                    if (!__any_sync(0xFFFFFFFFu, bad)) gok |= 1u << (2 * g + qq);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < kSumChunk / 32; ++g) {
+                const int g0 = beg + g * 32;
+                if (hit || g0 >= end) continue;
+                const uint32_t gb = __float_as_uint(s) & 0x7FFFFFFFu;
+                const uint32_t gbi = max(gb >> 23, 1u);
+                const int gq = static_cast<int>(gbi) - 127 - e;
+                if (gq >= 0 && gq < 2 && ((gok >> (2 * g + gq)) & 1u)) {
+                    const unsigned long long nb = gb + static_cast<unsigned long long>(gq ? gr[g][1] : gr[g][0]);
+                    if (nb < (static_cast<unsigned long long>(gbi + 1u) << 23)) {
+                        const float t = __uint_as_float(static_cast<uint32_t>(nb));
+                        if (!(t >= stop)) {
+                            s = t;
+                            continue;
                         }
                     }
                 }
-            }
-            for (; i < end && !hit; ++i) {
-                s = __fadd_rn(s, x(i));
-                if (s >= stop) {
-                    pos = i + 1;
-                    hit = true;
-                }
+                walk_group(v[g], g0, min(32, end - g0), s, stop, pos, hit);
             }
         }
-        sh->sum = s;
-        sh->at = pos;
+        if (lane == 0) {
+            sh->sum = s;
+            sh->at = pos;
+        }
     }
     __syncthreads();
     *at = sh->at;
@@ -280,14 +364,15 @@ __device__ __forceinline__ float exact_seq_sum(const float* x, int n, SumShared*
 // keep a prefix of the (p desc, id asc) order, so only a prefix that holds
 // the cut needs sorting. The probabilities are binned by their 12 leading
 // bits (exponent and 4 mantissa bits: bins are value ranges, descending bin
-// order is descending p), with each bin's count and exact mass (the integer
-// sum of its significands). The prefix is every bin down to
+// order is descending p) and counted per warp. The prefix is every bin down to
 //   min_p: the bin of min_p * p_max (every p >= the floor is above it; top_p
 //          either cuts inside it or not before min_p does);
-//   top_p: the first bin where the exact mass M of the bins above, counting c
-//          entries, has M * (1 - c * 2^-23) >= top_p (then the reference's
-//          sequential f32 cumulative, within (c-1) * 2^-24 * M of M, reaches
-//          top_p inside the prefix);
+//   top_p: the first bin where a lower bound M of the mass of the bins
+//          above, counting c entries, has M * (1 - c * 2^-23) >= top_p (then
+//          the reference's sequential f32 cumulative, within (c-1) * 2^-24 * M
+//          of the mass, reaches top_p inside the prefix); M is the larger of
+//          the sum of count * bin floor and the sum of every p less the sum of
+//          count * bin ceiling below;
 // the smaller of the two when both apply, else the whole row. The prefix is
 // scattered to K grouped by bin, cut at bin boundaries into segments of at
 // most kSegCap keys, and each segment is sorted in shared memory, so K holds
@@ -300,7 +385,6 @@ constexpr int kMaxSegs = kSumMaxChunks * kSumChunk / kSegStep + 1;
 
 struct FastShared {
     SumShared sum;
-    unsigned long long mant[kBins];  // per bin: sum of 24-bit significands
     unsigned int cnt[kBins];         // per bin: entries, then the next write position in K
     int bnd[kMaxSegs + 1];           // segment j starts at bnd[j]
     int lo_bin, lo_min, m, nseg, fail;
@@ -335,9 +419,12 @@ __device__ __forceinline__ uint32_t sig24(uint32_t pb) {  // p = sig24 * 2^(max(
     return (pb >> 23) ? ((pb & 0x7FFFFFu) | 0x800000u) : pb;
 }
 
-__device__ __forceinline__ double bin_mass(unsigned long long mant, int bin) {
-    const int ex = bin >> 4;
-    return ldexp(static_cast<double>(mant), (ex ? ex : 1) - 150);
+// The value range [bin_low, bin_low of bin + 1) of a bin of p's 12 leading bits.
+__device__ __forceinline__ double bin_low(int bin) {  // the float whose 12 leading bits are bin
+    return static_cast<double>(__uint_as_float(static_cast<uint32_t>(bin) << 19));
+}
+__device__ __forceinline__ double bin_high(int bin) {  // finite bins only; probabilities never exceed 1
+    return bin < 4079 ? bin_low(bin + 1) : 0.0;
 }
 
 // filter_row's result for a qualifying row (see above). Returns false, having
@@ -360,37 +447,61 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
     for (int j = tid; j < V; j += NT) lmax = fmaxf(lmax, W[j]);
     const float mx = block_max(lmax, red);
     bool bad = false;
-    for (int j = tid; j < V; j += NT) {
-        const float e = exp_f32(__fdiv_rn(__fsub_rn(W[j], mx), p.temperature));
-        E[j] = e;
-        bad |= !isfinite(e);
+    for (int j0 = 0; j0 < V; j0 += NT * kBatch) {
+        float w[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int j = j0 + q * NT + tid;
+            w[q] = j < V ? W[j] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int j = j0 + q * NT + tid;
+            if (j < V) {
+                const float e = exp_f32(__fdiv_rn(__fsub_rn(w[q], mx), p.temperature));
+                E[j] = e;
+                bad |= !isfinite(e);
+            }
+        }
     }
     if (__syncthreads_or(bad)) return false;
     const float total = exact_seq_sum<NT>(E, V, &fs->sum);
     // the largest exponential is exp(0) = 1, so p_max = 1 / total
     const float pmax = total > 0.0f ? __fdiv_rn(1.0f, total) : 1.0f;
-    // ---- bins: counts and exact masses ------------------------------------
-    for (int i = tid; i < kBins; i += NT) {
-        fs->cnt[i] = 0u;
-        fs->mant[i] = 0ull;
-    }
+    // ---- bins: counts (per warp, 16-bit, in sk) and the sum of p ---------
+    static_assert(NT / 32 * kBins * 2 <= kSegCap * 8, "per-warp bin counts must fit in sk");
+    unsigned int* hw = reinterpret_cast<unsigned int*>(sk);
+    for (int i = tid; i < NT / 32 * kBins / 2; i += NT) hw[i] = 0u;
     __syncthreads();
-    for (int j0 = 0; j0 < V; j0 += NT) {
-        const int j = j0 + tid;
-        const bool in = j < V;
-        uint32_t pb = 0u;
-        if (in) pb = __float_as_uint(total > 0.0f ? __fdiv_rn(E[j], total) : E[j]);
-        const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
-        if (in) {
-            const uint32_t bin = pb >> 19;
-            const unsigned peers = __match_any_sync(act, bin);
-            const unsigned msum = __reduce_add_sync(peers, sig24(pb));
-            if (lane == __ffs(peers) - 1) {
-                atomicAdd(&fs->cnt[bin], static_cast<unsigned>(__popc(peers)));
-                atomicAdd(&fs->mant[bin], static_cast<unsigned long long>(msum));
+    unsigned int* my = hw + warp * (kBins / 2);
+    double psum = 0.0;
+    for (int j0 = 0; j0 < V; j0 += NT * kBatch) {
+        float ev[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int j = j0 + q * NT + tid;
+            ev[q] = j < V ? E[j] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            if (j0 + q * NT + tid < V) {
+                const float pj = total > 0.0f ? __fdiv_rn(ev[q], total) : ev[q];
+                const uint32_t bin = __float_as_uint(pj) >> 19;
+                atomicAdd(my + (bin >> 1), 1u << ((bin & 1u) * 16u));
+                psum += pj;
             }
         }
     }
+    psum = warp_sum_f64(psum);
+    if (lane == 0) fs->sum.d[warp] = psum;
+    __syncthreads();
+    for (int b = tid; b < kBins; b += NT) {
+        unsigned c = 0u;
+        for (int w = 0; w < NT / 32; ++w) c += (hw[w * (kBins / 2) + (b >> 1)] >> ((b & 1) * 16)) & 0xFFFFu;
+        fs->cnt[b] = c;
+    }
+    double ptot = 0.0;  // the sum of every p, within 2^-40 relative
+    for (int w = 0; w < NT / 32; ++w) ptot += fs->sum.d[w];
     __syncthreads();
     // ---- the prefix's lowest bin, positions and segments (warp 0) ---------
     if (warp == 0) {
@@ -403,32 +514,44 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
         }
         int lo_top = -1;
         if (top_p_on) {
-            double ml = 0.0;
+            // mass(bins >= b) is at least max(sum c*low, ptot - sum below b of
+            // c*high); the prefix is certified where that bound * (1 - c 2^-23)
+            // reaches top_p
+            double al = 0.0, ah = 0.0;
             unsigned cl = 0u;
             for (int i = 0; i < kPer; ++i) {
-                ml += bin_mass(fs->mant[top - i], top - i);
-                cl += fs->cnt[top - i];
+                const int b = top - i;
+                const double c = static_cast<double>(fs->cnt[b]);
+                al += c * bin_low(b);
+                ah += c * bin_high(b);
+                cl += fs->cnt[b];
             }
-            double mi = ml;
+            double il = al, ih = ah;
             unsigned ci = cl;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const double y = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+                const double y = __shfl_up_sync(0xFFFFFFFFu, il, o);
+                const double yh = __shfl_up_sync(0xFFFFFFFFu, ih, o);
                 const unsigned z = __shfl_up_sync(0xFFFFFFFFu, ci, o);
                 if (lane >= o) {
-                    mi += y;
+                    il += y;
+                    ih += yh;
                     ci += z;
                 }
             }
-            double mm = mi - ml;
+            const double hall = __shfl_sync(0xFFFFFFFFu, ih, 31);
+            double ml = il - al, mh = ih - ah;
             unsigned cc = ci - cl;
             int found = -1;
             for (int i = 0; i < kPer && found < 0; ++i) {
-                const unsigned c = fs->cnt[top - i];
-                mm += bin_mass(fs->mant[top - i], top - i);
+                const int b = top - i;
+                const unsigned c = fs->cnt[b];
+                ml += static_cast<double>(c) * bin_low(b);
+                mh += static_cast<double>(c) * bin_high(b);
                 cc += c;
-                if (c != 0u && mm * (1.0 - ldexp(static_cast<double>(cc), -23)) >= static_cast<double>(p.top_p))
-                    found = top - i;
+                const double lb = fmax(ml, ptot * (1.0 - 0x1p-40) - (hall - mh));
+                if (c != 0u && lb * (1.0 - ldexp(static_cast<double>(cc), -23)) >= static_cast<double>(p.top_p))
+                    found = b;
             }
             const unsigned bal = __ballot_sync(0xFFFFFFFFu, found >= 0);
             if (bal) lo_top = __shfl_sync(0xFFFFFFFFu, found, __ffs(bal) - 1);
@@ -481,24 +604,28 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
     if (fs->fail) return false;
     const int lo_bin = fs->lo_bin, m = fs->m, nseg = fs->nseg;
     // ---- scatter the prefix to K, grouped by bin --------------------------
-    for (int j0 = 0; j0 < V; j0 += NT) {
-        const int j = j0 + tid;
-        float pj = 0.0f;
-        bool take = false;
-        uint32_t bin = 0u;
-        if (j < V) {
-            pj = total > 0.0f ? __fdiv_rn(E[j], total) : E[j];
-            bin = __float_as_uint(pj) >> 19;
-            take = static_cast<int>(bin) >= lo_bin;
+    for (int j0 = 0; j0 < V; j0 += NT * kBatch) {
+        float ev[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int j = j0 + q * NT + tid;
+            ev[q] = j < V ? E[j] : 0.0f;
         }
-        const unsigned act = __ballot_sync(0xFFFFFFFFu, take);
-        if (take) {
-            const unsigned peers = __match_any_sync(act, bin);
-            const int leader = __ffs(peers) - 1;
-            unsigned base = 0u;
-            if (lane == leader) base = atomicAdd(&fs->cnt[bin], static_cast<unsigned>(__popc(peers)));
-            base = __shfl_sync(peers, base, leader);
-            K[base + __popc(peers & ((1u << lane) - 1u))] = make_key(order32(pj), static_cast<uint32_t>(j));
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int j = j0 + q * NT + tid;
+            const float pj = total > 0.0f ? __fdiv_rn(ev[q], total) : ev[q];
+            const uint32_t bin = __float_as_uint(pj) >> 19;
+            const bool take = j < V && static_cast<int>(bin) >= lo_bin;
+            const unsigned act = __ballot_sync(0xFFFFFFFFu, take);
+            if (take) {
+                const unsigned peers = __match_any_sync(act, bin);
+                const int leader = __ffs(peers) - 1;
+                unsigned base = 0u;
+                if (lane == leader) base = atomicAdd(&fs->cnt[bin], static_cast<unsigned>(__popc(peers)));
+                base = __shfl_sync(peers, base, leader);
+                K[base + __popc(peers & ((1u << lane) - 1u))] = make_key(order32(pj), static_cast<uint32_t>(j));
+            }
         }
     }
     __syncthreads();

@@ -42,7 +42,7 @@ __device__ __forceinline__ bool is_general(const SampleArgs& a, int row, const t
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kGenThreads) general_kernel(SampleArgs a, GeneralScratch g) {
+__global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, GeneralScratch g) {
     __shared__ float red[kGenThreads / 32];
     __shared__ int sh_int[4];
     __shared__ FilterOut fo;

@@ -93,7 +93,7 @@ struct MergeArgs {
 struct MtpScratch {
     float* work;               // logits, then candidate tokens
     float* e;                  // exponentials
-    unsigned long long* keys;  // probability keys, then residual lists
+    unsigned long long* keys;  // probability keys
     size_t stride;             // floats per workspace in work / e
     size_t key_stride;         // keys per list (a power of two >= vocab)
 };

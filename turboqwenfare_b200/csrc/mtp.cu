@@ -39,7 +39,6 @@ struct Workspace {
     float* W;
     float* E;
     unsigned long long* K;
-    unsigned long long* R;  // residual lists (tokens ascending)
 };
 
 __device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta, int which) {
@@ -47,8 +46,7 @@ __device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta, int
     const size_t slot = static_cast<size_t>(cta) * 2 + which;
     w.W = g.work + slot * g.stride;
     w.E = g.e + slot * g.stride;
-    w.K = g.keys + slot * g.key_stride * 2;
-    w.R = w.K + g.key_stride;
+    w.K = g.keys + slot * g.key_stride;
     return w;
 }
 
@@ -85,63 +83,77 @@ __device__ void q_of(const Workspace& w, const FilterOut& fo, int x, int vocab, 
     __syncthreads();
 }
 
-// Writes the row's nonzero q as keys sorted by ascending token into w.R
-// (key = (~token << 32) | bits(q), sorted descending); returns the count.
-__device__ int q_list(const Workspace& w, const FilterOut& fo) {
-    const bool point = !(isfinite(fo.total2) && fo.total2 > 0.0f);
-    const int n = point ? 1 : fo.keep;
-    const int n2 = pow2_at_least(n);
-    for (int i = threadIdx.x; i < n2; i += kMT) {
-        unsigned long long key = 0ull;
-        if (i < n) {
-            const uint32_t tok = key_token(w.K[i]);
-            const float q = point ? 1.0f : __fdiv_rn(key_value(w.K[i]), fo.total2);
-            key = (static_cast<unsigned long long>(0xFFFFFFFFu - tok) << 32) | __float_as_uint(q);
-        }
-        w.R[i] = key;
+// q of a filter_row result for every id, dense in w.W (free once filter_row
+// has run): zero except the kept ids.
+__device__ void q_dense(const Workspace& w, const FilterOut& fo, int vocab) {
+    float* Q = w.W;
+    for (int i = threadIdx.x; i < vocab; i += kMT) Q[i] = 0.0f;
+    __syncthreads();
+    if (!(isfinite(fo.total2) && fo.total2 > 0.0f)) {
+        if (threadIdx.x == 0 && fo.keep > 0) Q[key_token(w.K[0])] = 1.0f;
+    } else {
+        for (int i = threadIdx.x; i < fo.keep; i += kMT)
+            Q[key_token(w.K[i])] = __fdiv_rn(key_value(w.K[i]), fo.total2);
     }
     __syncthreads();
-    bitonic_desc(w.R, n2);
-    return n;
 }
 
-// The residual draw (see the file comment) by one thread over the two
-// ascending-token lists; -1 when the residual mass is zero.
-__device__ int residual_token(const unsigned long long* rt, int nt, const unsigned long long* rd,
-                              int nd, float u) {
-    unsigned long long total = 0ull;
-    for (int pass = 0; pass < 2; ++pass) {
-        unsigned long long thr = 0ull, pre = 0ull;
-        if (pass == 1) {
-            if (total == 0ull) return -1;
-            const unsigned long long uq = static_cast<unsigned long long>(ldexp(static_cast<double>(u), 32));
-            const unsigned long long lo = uq * total, hi = __umul64hi(uq, total);
-            thr = (hi << 32) | (lo >> 32);
-        }
-        int i = 0, j = 0;
-        while (i < nt || j < nd) {
-            const uint32_t ti = i < nt ? 0xFFFFFFFFu - static_cast<uint32_t>(rt[i] >> 32) : 0xFFFFFFFFu;
-            const uint32_t tj = j < nd ? 0xFFFFFFFFu - static_cast<uint32_t>(rd[j] >> 32) : 0xFFFFFFFFu;
-            const uint32_t tok = ti < tj ? ti : tj;
-            float qt = 0.0f, qd = 0.0f;
-            if (i < nt && ti == tok) qt = __uint_as_float(static_cast<uint32_t>(rt[i++]));
-            if (j < nd && tj == tok) qd = __uint_as_float(static_cast<uint32_t>(rd[j++]));
-            const float d = __fsub_rn(qt, qd);
-            const unsigned long long r =
-                d > 0.0f ? __double2ull_rn(ldexp(static_cast<double>(d), 62)) : 0ull;
-            if (pass == 0) {
-                total += r;
-            } else {
-                pre += r;
-                if (pre > thr) return static_cast<int>(tok);
+// An id's residual max(0, q_target - q_draft) as a multiple of 2^-62.
+__device__ __forceinline__ unsigned long long residual_units(const float* QT, const float* QD, int t) {
+    const float d = __fsub_rn(QT[t], QD[t]);
+    return d > 0.0f ? __double2ull_rn(ldexp(static_cast<double>(d), 62)) : 0ull;
+}
+
+// The residual draw (see the file comment) over the dense q arrays. The
+// residuals are integers, so their prefix over ascending ids is exact in any
+// order: each thread sums a contiguous range of ids, a block scan gives the
+// ranges' offsets, and the thread whose range holds the first prefix above
+// thr walks it. Returns -1 (to every thread) when the residual mass is zero.
+__device__ int residual_token(const float* QT, const float* QD, int vocab, float u,
+                              unsigned long long* wsum, int* shared_word) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (vocab + kMT - 1) / kMT;
+    const int t0 = min(vocab, tid * per), t1 = min(vocab, t0 + per);
+    unsigned long long loc = 0ull;
+    for (int t = t0; t < t1; ++t) loc += residual_units(QT, QD, t);
+    unsigned long long inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (threadIdx.x == 0) *shared_word = -1;
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    unsigned long long before = 0ull, total = 0ull;
+    for (int w = 0; w < kMT / 32; ++w) {
+        if (w < warp) before += wsum[w];
+        total += wsum[w];
+    }
+    const unsigned long long excl = before + inc - loc;
+    if (total != 0ull) {
+        const unsigned long long uq = static_cast<unsigned long long>(ldexp(static_cast<double>(u), 32));
+        const unsigned long long lo = uq * total, hi = __umul64hi(uq, total);
+        const unsigned long long thr = (hi << 32) | (lo >> 32);  // floor(uq * total / 2^32) < total
+        if (excl <= thr && thr < excl + loc) {
+            unsigned long long pre = excl;
+            for (int t = t0; t < t1; ++t) {
+                pre += residual_units(QT, QD, t);
+                if (pre > thr) {
+                    *shared_word = t;
+                    break;
+                }
             }
         }
     }
-    return -1;
+    __syncthreads();
+    const int r = *shared_word;
+    __syncthreads();
+    return r;
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kMT) mtp_kernel(MtpArgs m, MtpScratch g) {
+__global__ void __launch_bounds__(kMT, 1) mtp_kernel(MtpArgs m, MtpScratch g) {
     __shared__ float red[kMT / 32];
     __shared__ unsigned long long redk[kMT / 32];
     __shared__ FilterOut ft, fd;
@@ -190,16 +202,10 @@ __global__ void __launch_bounds__(kMT) mtp_kernel(MtpArgs m, MtpScratch g) {
                 ok = __fmul_rn(us[j], qv[1]) < qv[0];
                 if (!ok && accepted < 0) {
                     accepted = j;
-                    const int nt = q_list(A, ft);
-                    const int nd = q_list(B, fd);
-                    if (tid == 0) {
-                        int t = residual_token(A.R, nt, B.R, nd, us[L]);
-                        if (t < 0) t = draw_kept(A.K, ft.keep, ft.total2, us[L]);
-                        sh[0] = t;
-                    }
-                    __syncthreads();
-                    token = sh[0];
-                    __syncthreads();
+                    q_dense(A, ft, m.vocab);
+                    q_dense(B, fd, m.vocab);
+                    token = residual_token(A.W, B.W, m.vocab, us[L], redk, &sh[0]);
+                    if (token < 0) token = draw_row<kMT>(A.K, ft, us[L], fs, &sh[0]);
                 }
             }
             if (tid == 0 && m.out_mask != nullptr) m.out_mask[drow0 + j] = ok ? 1 : 0;
@@ -231,8 +237,8 @@ size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride
     size_t p2 = 1;
     while (p2 < v) p2 <<= 1;
     *key_stride = p2;
-    // per CTA two workspaces: W and E (stride floats each), K and R (p2 keys each)
-    return static_cast<size_t>(ctas) * 2 * (*stride * 8 + *key_stride * 16);
+    // per CTA two workspaces: W and E (stride floats each) and K (p2 keys)
+    return static_cast<size_t>(ctas) * 2 * (*stride * 8 + *key_stride * 8);
 }
 
 cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s) {
