@@ -46,6 +46,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--vocab-shard", action="store_true",
+                    help="configuration 4's vocabulary split over the ranks (NCCL all-gather of "
+                         "per-shard top-k) instead of row sharding")
     return ap.parse_args()
 
 
@@ -336,10 +339,89 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_vocab_sharded(args):
+    """Configuration 4: every rank holds all rows' ids [offset, offset + V/N);
+    one step = export, NCCL all-gather, merge and draw on every rank. Total
+    work is fixed as N grows (strong scaling)."""
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from turboqwenfare_b200 import workloads as W
+    from turboqwenfare_b200.sampler import params_tensor
+    from turboqwenfare_b200.sharding import NcclComm, sample_vocab_sharded, vocab_shards
+    batch = W.config("c4", seed=args.seed)  # the same rows on every rank
+    off0, n = vocab_shards(batch.vocab, world)[rank]
+    full = torch.from_numpy(batch.logits.view(np.int16)).view(torch.bfloat16)
+    nbuf = max(1, math.ceil(2 * L2_BYTES / (batch.rows * n * 2)) + 1)
+    bufs = [torch.roll(full, shifts=i * 977, dims=1)[:, off0:off0 + n].contiguous().to(dev) for i in range(nbuf)]
+    hist = torch.from_numpy(batch.hist).to(dev)
+    hoff = torch.from_numpy(batch.hist_off).to(dev)
+    params = params_tensor(batch.params, batch.rows, dev)
+    uni = torch.from_numpy(batch.uniforms).to(dev)
+    if world > 1:
+        comm = NcclComm(rank, world, local)
+    else:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % _free_port(), rank=0, world_size=1)
+        comm = NcclComm(0, 1, local)
+
+    def step(i):
+        sample_vocab_sharded(comm, bufs[i % nbuf], params, off0, batch.vocab, uniforms=uni, history=hist,
+                             history_offsets=hoff)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clk = clocks.stop()
+    ms_per_step = ms / args.steps
+    alg = batch.rows * batch.vocab * 2 + 4 * int(batch.hist_off[-1]) * world
+    line = {
+        "metric": "sampled rows/sec at V=151,936", "value": round(batch.rows * args.steps / (ms / 1000.0), 1),
+        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "c4", "rows": batch.rows, "vocab": batch.vocab, "vocab_per_gpu": n,
+                   "parallelism": f"vocabulary split over {world} GPU(s), NCCL all-gather of per-shard top-50",
+                   "l2": f"{nbuf} rotating input buffers", "seed": args.seed},
+        "hbm_gbs_whole_step": round(alg / world / (ms_per_step / 1000.0) / 1e9, 1),
+        "gpu_launches": args.steps * 3, "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    comm.close()
+    import torch.distributed as dist
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def _free_port():
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.vocab_shard:
+        run_vocab_sharded(args)
     else:
         run_ours(args)
 
