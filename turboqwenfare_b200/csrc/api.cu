@@ -48,13 +48,14 @@ struct TimedLaunch {
 
 }  // namespace
 
+constexpr int kTimingKinds = 5;  // stream, general, window, MTP, finalize
+
 struct tqfs_handle {
     int device = 0;
     std::string error;
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
     DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
-    DeviceBuffer tickets;      // per-row unit tickets, tagged with the call's number
     DeviceBuffer mtp;          // MTP verify workspaces
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
@@ -66,8 +67,8 @@ struct tqfs_handle {
     bool timing = false;
     std::vector<TimedLaunch> pending;
     std::vector<cudaEvent_t> free_events;
-    double kernel_ms[4] = {0, 0, 0, 0};
-    long long launches[4] = {0, 0, 0, 0};
+    double kernel_ms[kTimingKinds] = {};
+    long long launches[kTimingKinds] = {};
 };
 
 struct tqfs_sampler {
@@ -165,14 +166,8 @@ int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::Sampl
         if (e == cudaSuccess) e = cudaMemset(h->err_word.ptr, 0, 16);
         if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     }
-    if (h->tickets.bytes < static_cast<size_t>(rows) * 8) {  // new memory starts at zero
-        e = h->tickets.reserve(static_cast<size_t>(rows) * 8);
-        if (e == cudaSuccess) e = cudaMemset(h->tickets.ptr, 0, h->tickets.bytes);
-        if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
-    }
     if (++h->epoch == 0u) h->epoch = 1u;
     a.err_word = static_cast<uint32_t*>(h->err_word.ptr);
-    a.ticket = static_cast<unsigned long long*>(h->tickets.ptr);
     a.epoch = h->epoch;
     return TQFS_OK;
 }
@@ -202,6 +197,10 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
         if (e == cudaSuccess) {
             TimingScope ts(h, s, 0);
             e = tqfs::launch_stream(a, plan, s, window && !h->timing);
+        }
+        if (e == cudaSuccess) {
+            TimingScope ts(h, s, 4);
+            e = tqfs::launch_finalize(a, plan, s, !h->timing);
         }
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
@@ -306,7 +305,6 @@ int tqfs_destroy(tqfs_handle* h) {
     h->scratch.release();
     h->general.release();
     h->err_word.release();
-    h->tickets.release();
     h->mtp.release();
     h->shard_send.release();
     h->shard_recv.release();
@@ -328,7 +326,7 @@ int tqfs_set_timing(tqfs_handle* h, int enabled) {
     if (!h) return TQFS_ERR_INVALID_ARG;
     drain_timing(h);
     h->timing = enabled != 0;
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kTimingKinds; ++i) {
         h->kernel_ms[i] = 0.0;
         h->launches[i] = 0;
     }
@@ -338,7 +336,7 @@ int tqfs_set_timing(tqfs_handle* h, int enabled) {
 int tqfs_get_timing(tqfs_handle* h, int n, float* kernel_ms, int64_t* launches) {
     if (!h || n < 0) return TQFS_ERR_INVALID_ARG;
     drain_timing(h);
-    for (int i = 0; i < n && i < 4; ++i) {
+    for (int i = 0; i < n && i < kTimingKinds; ++i) {
         if (kernel_ms) kernel_ms[i] = static_cast<float>(h->kernel_ms[i]);
         if (launches) launches[i] = h->launches[i];
     }
@@ -605,6 +603,10 @@ int tqfs_shard_export(tqfs_handle* h, const void* logits_dev, int dtype, int row
     if (e == cudaSuccess) {
         TimingScope ts(h, s, 0);
         e = tqfs::launch_stream(a, plan, s, hist_off_dev != nullptr && !h->timing);
+    }
+    if (e == cudaSuccess) {
+        TimingScope ts(h, s, 4);
+        e = tqfs::launch_finalize(a, plan, s, !h->timing);
     }
     return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "shard export launch");
 }

@@ -37,7 +37,6 @@ struct SampleArgs {
     int chunk_len;             // ids per chunk
     int unit_len;              // chunks per unit (a warp's run of one row)
     int units;                 // units per row
-    unsigned long long* ticket;  // rows: (epoch << 32) | units of the row done
     uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
     uint32_t epoch;            // this call's number (never 0)
     int vec_ok;                // rows start on 16-byte boundaries
@@ -116,6 +115,9 @@ size_t stream_scratch(int rows, const Plan& plan, void* base, SampleArgs* a);
 // after_window lets the stream kernel's launch overlap the pre-pass.
 cudaError_t launch_window(const SampleArgs& a, const Plan& plan, cudaStream_t s);
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool after_window);
+// Finalises the stream kernel's rows (one warp per row); `overlap` launches it
+// behind the stream grid (programmatic serialization).
+cudaError_t launch_finalize(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool overlap);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
 cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s);
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,

@@ -34,13 +34,11 @@ constexpr size_t kStaticBytes = static_cast<size_t>(48) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
 static __device__ uint32_t g_static_err;  // zero at load; see SampleArgs::epoch
 constexpr int kStaticRows = 4096;
-static __device__ unsigned long long g_static_ticket[kStaticRows];  // zero at load
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
 void* g_err_addr[kMaxDevices] = {};
-void* g_ticket_addr[kMaxDevices] = {};
 uint32_t g_epoch[kMaxDevices] = {};
 
 // Rows the stream kernel does not own (general rows) keep this status.
@@ -55,24 +53,19 @@ __global__ void mark_unhandled_kernel(int rows, int32_t* out_token, int32_t* out
 // symbol names a host-side stand-in, not device memory, so the address is
 // looked up once per device (with that device current) and cached.
 // Also hands out the call's epoch (never 0).
-cudaError_t static_scratch(int device, void** out, uint32_t** err, unsigned long long** ticket,
-                           uint32_t* epoch) {
+cudaError_t static_scratch(int device, void** out, uint32_t** err, uint32_t* epoch) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_scratch_addr[device] == nullptr) {
         void* ptr = nullptr;
         void* eptr = nullptr;
-        void* tptr = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e == cudaSuccess) e = cudaGetSymbolAddress(&eptr, g_static_err);
-        if (e == cudaSuccess) e = cudaGetSymbolAddress(&tptr, g_static_ticket);
         if (e != cudaSuccess) return e;
         g_scratch_addr[device] = ptr;
         g_err_addr[device] = eptr;
-        g_ticket_addr[device] = tptr;
     }
     *out = g_scratch_addr[device];
     *err = static_cast<uint32_t*>(g_err_addr[device]);
-    *ticket = static_cast<unsigned long long*>(g_ticket_addr[device]);
     if (++g_epoch[device] == 0u) g_epoch[device] = 1u;
     *epoch = g_epoch[device];
     return cudaSuccess;
@@ -103,9 +96,8 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
         return TQFS_ERR_NO_DEVICE;
     void* base = nullptr;
     uint32_t* err = nullptr;
-    unsigned long long* ticket = nullptr;
     uint32_t epoch = 0;
-    if (static_scratch(device, &base, &err, &ticket, &epoch) != cudaSuccess) return TQFS_ERR_CUDA;
+    if (static_scratch(device, &base, &err, &epoch) != cudaSuccess) return TQFS_ERR_CUDA;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     SampleArgs a{};
@@ -123,7 +115,6 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     a.out_status = out_status_dev;
     stream_scratch(rows, plan, base, &a);
     a.err_word = err;
-    a.ticket = ticket;
     a.epoch = epoch;
     const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = (reinterpret_cast<uintptr_t>(logits_dev) & 15u) == 0 &&
@@ -135,5 +126,6 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     if (cudaGetLastError() != cudaSuccess) return TQFS_ERR_CUDA;
     if (launch_window(a, plan, s) != cudaSuccess) return TQFS_ERR_CUDA;
     const bool window = hist_off_dev != nullptr;
-    return launch_stream(a, plan, s, window) == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
+    if (launch_stream(a, plan, s, window) != cudaSuccess) return TQFS_ERR_CUDA;
+    return launch_finalize(a, plan, s, true) == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
 }

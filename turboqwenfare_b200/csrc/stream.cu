@@ -59,11 +59,12 @@ constexpr int kListOff = 16384;   // per-warp shared memory: chunk buffers (+ ex
 constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins,
 constexpr int kSortOff = kBinsOff + 256 * 4;       // ranked keys of a finalised row
 constexpr int kWarpSmem = kSortOff + kStreamMaxK * 8;  // 21 KiB
-constexpr int kCasTries = 1 << 20;                 // attempts at a row ticket
 constexpr int kMaxUnits = 32;                      // units per row (one lane each)
 constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
 constexpr int kWinWarps = 8;      // warps of the window kernel
+constexpr int kFinWarps = 8;      // warps (rows) per CTA of the finalize kernel
+constexpr int kFinWarpSmem = kListCap * 8 + kStreamMaxK * 8 + 256 * 4;
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
 
 __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned long long k) {
@@ -294,11 +295,44 @@ __device__ __forceinline__ unsigned long long warp_min64(unsigned long long x) {
     return x;
 }
 
-// Keeps the min(n, k) largest of the n distinct keys L[0..n) in L[0..),
-// in any order, and returns the smallest kept key (0 when n == 0). Radix
-// select over 8-bit digits with a per-warp histogram in `bins`.
-__device__ __noinline__ unsigned long long warp_keep_top(unsigned long long* L, int* n_io, int k,
-                                                         unsigned int* bins) {
+// Keeps the k largest of the n (k < n <= 32 * R) distinct keys L[0..n) in
+// L[0..k), sorted descending, and returns the k-th. Each lane holds R keys in
+// registers and ranks them against every key of L (broadcast reads): a key's
+// rank is the number of larger keys, so the kept keys go straight to L[rank].
+template <int R>
+__device__ __forceinline__ unsigned long long warp_keep_top_rank(unsigned long long* L, int n, int k,
+                                                                 int lane) {
+    unsigned long long key[R];
+    int rank[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        key[r] = i < n ? L[i] : ~0ull;
+        rank[r] = 0;
+    }
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) {
+        const unsigned long long o = L[j];
+#pragma unroll
+        for (int r = 0; r < R; ++r) rank[r] += o > key[r] ? 1 : 0;
+    }
+    __syncwarp();
+    unsigned long long kth = 0ull;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (r * 32 + lane < n && rank[r] < k) {
+            L[rank[r]] = key[r];
+            if (rank[r] == k - 1) kth = key[r];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kth = umax64(kth, __shfl_xor_sync(0xFFFFFFFFu, kth, o));
+    __syncwarp();
+    return kth;
+}
+
+__device__ __noinline__ unsigned long long warp_keep_top_radix(unsigned long long* L, int* n_io, int k,
+                                                               unsigned int* bins) {
     const int lane = threadIdx.x & 31;
     const int n = *n_io;
     if (n <= k) {
@@ -374,6 +408,28 @@ __device__ __noinline__ unsigned long long warp_keep_top(unsigned long long* L, 
 }
 
 // The chunk's values from shared memory by id: f32, or bf16 widened.
+
+// Keeps the min(n, k) largest of the n distinct keys L[0..n) (n <= kListCap)
+// in L[0..), and returns the smallest kept key (0 when n == 0): by ranking
+// for up to 128 keys (the kept keys then sorted descending), else by radix
+// select (in any order).
+__device__ __noinline__ unsigned long long warp_keep_top(unsigned long long* L, int* n_io, int k,
+                                                         unsigned int* bins) {
+    const int lane = threadIdx.x & 31;
+    const int n = *n_io;
+    if (n <= k) {
+        unsigned long long mn = ~0ull;
+        for (int i = lane; i < n; i += 32) mn = umin64(mn, L[i]);
+        mn = warp_min64(mn);
+        return n > 0 ? mn : 0ull;
+    }
+    if (n > 128) return warp_keep_top_radix(L, n_io, k, bins);
+    __syncwarp();
+    *n_io = k;
+    if (n <= 64) return warp_keep_top_rank<2>(L, n, k, lane);
+    return warp_keep_top_rank<4>(L, n, k, lane);
+}
+
 template <bool F32>
 __device__ __forceinline__ float chunk_value(const void* v, int id) {
     if constexpr (F32) return static_cast<const float*>(v)[id];
@@ -484,12 +540,6 @@ __device__ __noinline__ int chunk_select(const void* vals, int n_here, int base_
     return k;
 }
 
-// Penalised value of one window id (mod.rs:139-146); out of line so the
-// many call sites stay small.
-__device__ __noinline__ float penalise_id(float v, uint32_t count, float rep, float freq, float pres) {
-    return penalise(v, count, rep, freq, pres);
-}
-
 // Per-lane maxima of the chunk's values (NaN ignored) by slot: a slot is 4
 // f32 ids, (j*32 + lane)*4 + 0..3, or 8 bf16 ids, (j*32 + lane)*8 + 0..7
 // (bf16 uses slots 0..7). Ids at or beyond n_here are left out.
@@ -529,45 +579,49 @@ __device__ __forceinline__ void slot_maxima(const void* vals, int n_here, int la
     }
 }
 
-// Appends the keys of the ids of this lane's slots in `mask` whose value
-// beats thr (v > thr, or v >= thr with `incl`); positions come from *counter
-// and only those below room are written.
-template <bool F32>
-__device__ __noinline__ void insert_slots(const void* vals, unsigned mask, int n_here, float thr,
-                                          bool incl, int base_id, unsigned long long* out,
-                                          int* counter, int room) {
+// Count (WRITE = false) or append (WRITE = true, from out[pos] on, below
+// room) the ids of this lane's slots in `mask` whose value beats thr (v > thr,
+// or v >= thr with `incl`). A slot is read again from shared memory only when
+// its maximum passed, which after a unit's first chunk is rare.
+template <bool F32, bool WRITE>
+__device__ __forceinline__ int scan_slots(const void* vals, unsigned mask, int n_here, float thr,
+                                          bool incl, int base_id, unsigned long long* out, int pos,
+                                          int room) {
     constexpr int PER = F32 ? 4 : 8;
     const int lane = threadIdx.x & 31;
+    int c = 0;
     while (mask != 0u) {
         const int j = __ffs(mask) - 1;
         mask &= mask - 1u;
         const int e0 = (j * 32 + lane) * PER;
+#pragma unroll
         for (int q = 0; q < PER; ++q) {
             const int id = e0 + q;
-            if (id < n_here) {
-                const float v = chunk_value<F32>(vals, id);
-                if (v > thr || (incl && v == thr)) {
-                    const int pos = atomicAdd(counter, 1);
-                    if (pos < room) out[pos] = make_key(order32(v), static_cast<uint32_t>(base_id + id));
-                }
+            const float v = chunk_value<F32>(vals, id);
+            if (id < n_here && (v > thr || (incl && v == thr))) {
+                if (WRITE && pos + c < room)
+                    out[pos + c] = make_key(order32(v), static_cast<uint32_t>(base_id + id));
+                ++c;
             }
         }
     }
+    return c;
 }
 
-// One chunk of a unit. With `sel` (the unit's exact k-th value th is known)
-// it appends the ids that beat th: ids only grow along a unit, so a later id
-// at the k-th value ranks below it and strict '>' is exact. Without it (the
+// One chunk of a unit. With `sel` the unit keeps the ids above th, a value at
+// or below the unit's k-th: ids only grow along a unit, so a later id equal to
+// th ranks below k earlier ones and strict '>' is exact. Without it (the
 // unit's first chunk) it appends the ids at or above theta, an order value
 // that k of them reach: the lane's slots are split into G groups (G = 1, 2, 4
 // for k <= 32, 64, 128) and a group's ceil(k/G)-th largest lane maximum is
 // reached by that many distinct ids, so the smallest of the G is reached by
-// k. Returns the number appended; -1 when the chunk needs the full selection
-// (too many ids reach theta, or fewer than k do).
+// k; theta becomes the unit's th. Appends go to out[0..room) at positions
+// from a warp scan of the lanes' counts. Returns the number appended; -1 when
+// the chunk needs the full selection (more ids than room, or fewer than k
+// reach theta).
 template <bool F32>
-__device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel, float th, int k,
-                                          int base_id, unsigned long long* out, int* counter,
-                                          int room) {
+__device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel, float& th, int k,
+                                          int base_id, unsigned long long* out, int room) {
     const int lane = threadIdx.x & 31;
     float sm[kSlots];
     slot_maxima<F32>(vals, n_here, lane, sm);
@@ -595,32 +649,14 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
     for (int j = 0; j < kSlots; ++j)
         mask |= static_cast<unsigned>(sel ? sm[j] > thr : sm[j] >= thr) << j;
     if (!__any_sync(0xFFFFFFFFu, mask != 0u)) return 0;
-    if (lane == 0) *counter = 0;
+    const int mine = mask ? scan_slots<F32, false>(vals, mask, n_here, thr, !sel, base_id, out, 0, room) : 0;
+    const int excl = warp_excl_scan(mine, lane);
+    const int total = __shfl_sync(0xFFFFFFFFu, excl + mine, 31);
+    if (total > room || (!sel && total < k)) return -1;
+    if (mask) scan_slots<F32, true>(vals, mask, n_here, thr, !sel, base_id, out, excl, room);
     __syncwarp();
-    if (mask != 0u) insert_slots<F32>(vals, mask, n_here, thr, !sel, base_id, out, counter, room);
-    __syncwarp();
-    const int c = *counter;
-    if (!sel && (c > room || c < k)) return -1;
-    return c;
-}
-
-// Claims one of the row's units: tickets hold (epoch << 32) | units done, so
-// a word left by an earlier call (same row, other epoch) counts as zero.
-// True for the claim that completes the row. A word that cannot be updated
-// within kCasTries attempts marks the call as failed.
-__device__ __forceinline__ bool row_ticket(const SampleArgs& a, int row) {
-    unsigned long long* t = a.ticket + row;
-    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(t);
-    for (int i = 0; i < kCasTries; ++i) {
-        const unsigned long long nv = (old >> 32) == a.epoch
-                                          ? old + 1ull
-                                          : (static_cast<unsigned long long>(a.epoch) << 32) | 1ull;
-        const unsigned long long prev = atomicCAS(t, old, nv);
-        if (prev == old) return static_cast<int>(nv & 0xFFFFFFFFull) == a.units;
-        old = prev;
-    }
-    atomicMax(a.err_word, a.epoch);
-    return false;
+    if (!sel) th = thr;
+    return total;
 }
 
 // Ranks the n distinct keys src[0..n) descending into dst (warp).
@@ -630,10 +666,62 @@ __device__ __forceinline__ void warp_rank_sort(const unsigned long long* src, in
     for (int i = lane; i < n; i += 32) {
         const unsigned long long key = src[i];
         int r = 0;
+#pragma unroll 8
         for (int j = 0; j < n; ++j) r += src[j] > key;
         dst[r] = key;
     }
     __syncwarp();
+}
+
+// The min(n, k) largest of the n (<= 128) distinct keys src[0..n), sorted
+// descending into dst (warp): each key's rank is the number of larger keys.
+__device__ __forceinline__ int warp_top_sorted(const unsigned long long* src, int n, int k,
+                                               unsigned long long* dst) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long key[4];
+    int rank[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        key[r] = r * 32 + lane < n ? src[r * 32 + lane] : ~0ull;
+        rank[r] = 0;
+    }
+#pragma unroll 8
+    for (int j = 0; j < n; ++j) {
+        const unsigned long long o = src[j];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) rank[r] += o > key[r] ? 1 : 0;
+    }
+    const int kk = n < k ? n : k;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        if (r * 32 + lane < n && rank[r] < kk) dst[rank[r]] = key[r];
+    __syncwarp();
+    return kk;
+}
+
+// A stop value no sum reaches (comparisons with NaN are false).
+__device__ __forceinline__ float no_stop() { return __int_as_float(0x7FC00000); }
+
+// Lane 0: the first position (1-based count) at which the sequential f32 sum
+// of x[0..n) from `init` reaches stop (n when it never does), and the sum
+// there. Loads go out eight at a time ahead of the adds.
+__device__ __forceinline__ int seq_scan(const float* x, int n, float init, float stop, float* sum) {
+    float c = init;
+    int at = n;
+    for (int i0 = 0; i0 < n && at == n; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = i0 + q < n ? x[i0 + q] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (at == n && i0 + q < n) {
+                c = __fadd_rn(c, v[q]);
+                if (c >= stop) at = i0 + q + 1;
+            }
+        }
+    }
+    *sum = c;
+    return at;
 }
 
 // The exact top-k by (value desc, id asc) of the n candidate keys L[0..n)
@@ -647,9 +735,25 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
                                            const float* uniforms, uint64_t* rng_state, int row,
                                            float* out_probs_row) {
     const int lane = threadIdx.x & 31;
-    warp_keep_top(L, &n, k, bins);
-    const int kk = n;  // min(k, candidates)
-    warp_rank_sort(L, kk, S);
+    // The draw's uniform (or generator state) travels while the rest runs.
+    float u_in = 0.0f;
+    uint64_t st[4] = {0ull, 0ull, 0ull, 0ull};
+    if (lane == 0) {
+        if (uniforms != nullptr) {
+            u_in = __ldg(uniforms + row);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st[q] = rng_state[static_cast<size_t>(row) * 4 + q];
+        }
+    }
+    int kk;
+    if (n <= 128) {
+        kk = warp_top_sorted(L, n, k, S);
+    } else {
+        warp_keep_top(L, &n, k, bins);
+        kk = n;  // min(k, candidates)
+        warp_rank_sort(L, kk, S);
+    }
     // softmax over the survivors (src/sampling/mod.rs:166-190)
     float* E = reinterpret_cast<float*>(L);                                  // kk floats
     unsigned long long* PK = L + kStreamMaxK / 2;                           // kk keys
@@ -659,29 +763,33 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
     for (int i = lane; i < kk; i += 32)
         E[i] = exp_f32(__fdiv_rn(__fsub_rn(key_value(S[i]), mx), p.temperature));
     __syncwarp();
-    float total_e = -0.0f;
-    if (lane == 0)
-        for (int i = 0; i < kk; ++i) total_e = __fadd_rn(total_e, E[i]);
+    float total_e = 0.0f;
+    if (lane == 0) seq_scan(E, kk, -0.0f, no_stop(), &total_e);
     total_e = __shfl_sync(0xFFFFFFFFu, total_e, 0);
+    for (int i = lane; i < kk; i += 32) P[i] = total_e > 0.0f ? __fdiv_rn(E[i], total_e) : E[i];
+    __syncwarp();
+    // The draw order is (p desc, id asc). p is non-increasing along S, so it
+    // differs from S's order only where distinct values share a p (or a p is
+    // NaN); only then are the probability keys ranked.
+    bool reorder = false;
     for (int i = lane; i < kk; i += 32) {
-        const float pv = total_e > 0.0f ? __fdiv_rn(E[i], total_e) : E[i];
-        PK[i] = make_key(order32(pv), key_token(S[i]));
+        const float pi = P[i];
+        reorder |= pi != pi;
+        if (i + 1 < kk) reorder |= P[i + 1] == pi && key_value(S[i + 1]) != key_value(S[i]);
     }
-    __syncwarp();
-    warp_rank_sort(PK, kk, S);  // probability keys in draw order
-    for (int i = lane; i < kk; i += 32) P[i] = key_value(S[i]);
-    __syncwarp();
+    if (__any_sync(0xFFFFFFFFu, reorder)) {
+        for (int i = lane; i < kk; i += 32) PK[i] = make_key(order32(P[i]), key_token(S[i]));
+        __syncwarp();
+        warp_rank_sort(PK, kk, S);  // probability keys in draw order
+        for (int i = lane; i < kk; i += 32) P[i] = key_value(S[i]);
+        __syncwarp();
+    }
     // top_p, min_p, draw (src/sampling/mod.rs:195-248)
     int keep = kk, token = 0;
     if (lane == 0) {
         if (!(p.top_p >= 1.0f)) {
-            float cum = 0.0f;
-            int c = 0;
-            for (int i = 0; i < kk; ++i) {
-                cum = __fadd_rn(cum, P[i]);
-                ++c;
-                if (cum >= p.top_p) break;
-            }
+            float cum;
+            const int c = seq_scan(P, kk, 0.0f, p.top_p, &cum);
             keep = c < 1 ? 1 : c;
             if (keep > kk) keep = kk;
         }
@@ -693,29 +801,17 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
         }
         if (keep > 0) {
             int pick = 0;
-            float total2 = -0.0f;
-            for (int i = 0; i < keep; ++i) total2 = __fadd_rn(total2, P[i]);
+            float total2;
+            seq_scan(P, keep, -0.0f, no_stop(), &total2);
             if (isfinite(total2) && total2 > 0.0f) {
-                float u;
-                if (uniforms != nullptr) {
-                    u = uniforms[row];
-                } else {
-                    uint64_t st[4];
-                    uint64_t* sp = rng_state + static_cast<size_t>(row) * 4;
-                    for (int q = 0; q < 4; ++q) st[q] = sp[q];
+                float u = u_in;
+                if (uniforms == nullptr) {
                     u = xoshiro_next_f32(st);
-                    for (int q = 0; q < 4; ++q) sp[q] = st[q];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) rng_state[static_cast<size_t>(row) * 4 + q] = st[q];
                 }
-                const float target = __fmul_rn(u, total2);
-                float cum = 0.0f;
-                pick = keep - 1;
-                for (int i = 0; i < keep; ++i) {
-                    cum = __fadd_rn(cum, P[i]);
-                    if (cum >= target) {
-                        pick = i;
-                        break;
-                    }
-                }
+                float cum;
+                pick = seq_scan(P, keep, 0.0f, __fmul_rn(u, total2), &cum) - 1;
             }
             token = static_cast<int>(key_token(S[pick]));
         }
@@ -738,7 +834,6 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
                                           unsigned long long* L, unsigned long long* S,
                                           unsigned int* bins, int* counter) {
     const int lane = threadIdx.x & 31;
-    __threadfence();  // the other units' lists are visible after their tickets
     const int U = a.units;
     const size_t base = static_cast<size_t>(row) * U;
     // Loads issued together: the lists' lengths and bounds, the row's knobs.
@@ -799,26 +894,35 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
         if (lane < U) offs[lane] = off_u;
         __syncwarp();
         // Gather the keys at or above the row bound (every row top-k member
-        // is one), keeping L short with exact top-k cuts.
+        // is one), keeping L short with exact top-k cuts. Each lane issues
+        // its loads of a batch together, so a batch costs one trip to L2.
+        constexpr int kGather = 4;
         int n = 0;
-        for (int q0 = 0; q0 < total; q0 += 32) {
-            const int q = q0 + lane;
-            unsigned long long key = 0ull;
-            bool keep = false;
-            if (q < total) {
-                int lo = 0, hi = U;  // the unit u with offs[u] <= q < offs[u + 1]
-                while (hi - lo > 1) {
-                    const int mid = (lo + hi) >> 1;
-                    if (offs[mid] <= q) lo = mid; else hi = mid;
+        for (int q0 = 0; q0 < total; q0 += 32 * kGather) {
+            unsigned long long key[kGather];
+#pragma unroll
+            for (int g = 0; g < kGather; ++g) {
+                const int q = q0 + g * 32 + lane;
+                key[g] = 0ull;
+                if (q < total) {
+                    int lo = 0, hi = U;  // the unit u with offs[u] <= q < offs[u + 1]
+                    while (hi - lo > 1) {
+                        const int mid = (lo + hi) >> 1;
+                        if (offs[mid] <= q) lo = mid; else hi = mid;
+                    }
+                    key[g] = __ldcg(a.cand + (base + lo) * kUnitCap + (q - offs[lo]));
                 }
-                key = __ldcg(a.cand + (base + lo) * kUnitCap + (q - offs[lo]));
-                keep = key >= kb;
             }
-            const unsigned ball = __ballot_sync(0xFFFFFFFFu, keep);
-            if (n + 32 > kListCap) warp_keep_top(L, &n, k, bins);
-            if (keep) L[n + __popc(ball & ((1u << lane) - 1u))] = key;
-            n += __popc(ball);
-            __syncwarp();
+#pragma unroll
+            for (int g = 0; g < kGather; ++g) {
+                const bool keep = q0 + g * 32 + lane < total && key[g] >= kb;
+                const unsigned ball = __ballot_sync(0xFFFFFFFFu, keep);
+                if (ball == 0u) continue;
+                if (n + 32 > kListCap) warp_keep_top(L, &n, k, bins);
+                if (keep) L[n + __popc(ball & ((1u << lane) - 1u))] = key[g];
+                n += __popc(ball);
+                __syncwarp();
+            }
         }
         if (rec != nullptr) {  // export: the shard's exact top-k, global ids
             warp_keep_top(L, &n, k, bins);
@@ -923,6 +1027,9 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
     // Launched right behind the window kernel: wait for its buckets (a no-op
     // when there is no window kernel in front).
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The finalize kernel behind this one may launch now (its CTAs find room
+    // as this grid's CTAs exit, and wait for the whole grid before reading).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int nw = static_cast<int>(gridDim.x) * kSW;
     const int nw_row = nw % a.rows, nw_u = nw / a.rows;
     const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
@@ -1085,7 +1192,7 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
                                          : i < 96 ? en[2]
                                          : i < 128 ? en[3] : __ldcg(src + i);
                         const uint32_t id = e >> 16;
-                        f[id] = penalise_id(f[id], e & 0xFFFFu, cur.pn.rep, cur.pn.freq, cur.pn.pres);
+                        f[id] = penalise(f[id], e & 0xFFFFu, cur.pn.rep, cur.pn.freq, cur.pn.pres);
                     }
                     __syncwarp();
                     vals = f;
@@ -1093,13 +1200,14 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
                 }
 
                 // ---- 3. the chunk's candidates, appended to L -------------
+                // The unit's first chunk keeps the ids at or above its theta
+                // (k of them reach it); later chunks keep what beats th.
                 const int room = kListCap - n;
-                const float th = sel ? from_order32(th_ord) : 0.0f;
-                int c = vals_f32
-                            ? unit_chunk<true>(vals, n_here, sel, th, k, base_id, L + n, &wcount[warp], room)
-                            : unit_chunk<false>(vals, n_here, sel, th, k, base_id, L + n, &wcount[warp], room);
-                bool full = !sel;
-                if (c >= 0 && !(sel && c > room)) {
+                float th = sel ? from_order32(th_ord) : 0.0f;
+                int c = vals_f32 ? unit_chunk<true>(vals, n_here, sel, th, k, base_id, L + n, room)
+                                 : unit_chunk<false>(vals, n_here, sel, th, k, base_id, L + n, room);
+                bool full = !sel;  // the first chunk's list defines the exact k-th
+                if (c >= 0) {
                     n += c;
                 } else {
                     // ---- 4. the full selection (overflow, ties, NaN) --------
@@ -1119,11 +1227,12 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
                 // ---- 6. unit end: its exact top-k and its k-th value -------
                 if (cur.last) {
                     const unsigned long long kth = warp_keep_top(L, &n, k, bins);
+                    const uint32_t theta = n >= k ? static_cast<uint32_t>(kth >> 32) : 0u;
                     unsigned long long* dst = a.cand + uslot * kUnitCap;
                     for (int i = lane; i < n; i += 32) dst[i] = L[i];
                     if (lane == 0) {
                         a.cand_n[uslot] = n;
-                        a.theta[uslot] = n >= k ? static_cast<uint32_t>(kth >> 32) : 0u;
+                        a.theta[uslot] = theta;
                     }
                     __syncwarp();
                     n = 0;
@@ -1131,15 +1240,6 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
                     th_ord = 0u;
                 }
             }
-        }
-        // ---- 7. the last unit of a row to finish finalises the row -------
-        if (cur.last && (cur.mode == kModeGreedy || cur.mode == kModeStream)) {
-            __threadfence();  // this unit's lists before its ticket
-            __syncwarp();
-            bool last = false;
-            if (lane == 0) last = row_ticket(a, cur.row);
-            if (__shfl_sync(0xFFFFFFFFu, last, 0))
-                finalize_row(a, cur.row, cur.mode == kModeGreedy, cur.k, L, S, bins, &wcount[warp]);
         }
         // Every value of the buffer has been read: refill it.
         __syncwarp();
@@ -1152,6 +1252,33 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
         nxt = nn;
         b ^= 1;
     }
+}
+
+// Finalises the rows the stream kernel owns, one warp per row, once every unit
+// list of the stream grid is written (launched behind it; griddepcontrol.wait
+// orders its reads after that grid's writes).
+__global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(SampleArgs a) {
+    extern __shared__ __align__(16) unsigned char fdyn[];
+    __shared__ int fcount[kFinWarps];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned char* wb = fdyn + static_cast<size_t>(warp) * kFinWarpSmem;
+    unsigned long long* L = reinterpret_cast<unsigned long long*>(wb);
+    unsigned long long* S = L + kListCap;
+    unsigned int* bins = reinterpret_cast<unsigned int*>(S + kStreamMaxK);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int row = static_cast<int>(blockIdx.x) * kFinWarps + warp;
+    if (row >= a.rows) return;
+    tqfs_params p{};
+    if (!a.top4_only) p = a.params[row];  // no parameters in the top-4 mode
+    long long hs = 0, he = 0, ws, wl;
+    if (a.hist_off != nullptr) {
+        hs = a.hist_off[row];
+        he = a.hist_off[row + 1];
+    }
+    const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
+    if (mode != kModeGreedy && mode != kModeStream) return;
+    (void)lane;
+    finalize_row(a, row, mode == kModeGreedy, static_cast<int>(p.top_k), L, S, bins, &fcount[warp]);
 }
 
 // Buckets the penalty window of every stream-sampled row by chunk and counts
@@ -1390,6 +1517,32 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     cfg.attrs = attr;
     cfg.numAttrs = after_window ? 1 : 0;  // overlap its launch with the window kernel
     return cudaLaunchKernelEx(&cfg, kern, a, top4_diag);
+}
+
+cudaError_t launch_finalize(const SampleArgs& a_in, const Plan& plan, cudaStream_t s, bool overlap) {
+    if (a_in.rows <= 0 || plan.units <= 0) return cudaSuccess;
+    const SampleArgs a = with_plan(a_in, plan);
+    const int fin_smem = kFinWarps * kFinWarpSmem;
+    static thread_local int fin_configured = -1;  // the device whose attribute is set
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (fin_configured != dev) {
+        e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem);
+        if (e != cudaSuccess) return e;
+        fin_configured = dev;
+    }
+    cudaLaunchConfig_t fc = {};
+    fc.gridDim = dim3(static_cast<unsigned>((a.rows + kFinWarps - 1) / kFinWarps));
+    fc.blockDim = dim3(kFinWarps * 32);
+    fc.dynamicSmemBytes = static_cast<size_t>(fin_smem);
+    fc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    fc.attrs = attr;
+    fc.numAttrs = overlap ? 1 : 0;  // launch behind the stream grid
+    return cudaLaunchKernelEx(&fc, finalize_kernel, a);
 }
 
 cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s) {
