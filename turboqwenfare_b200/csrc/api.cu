@@ -236,7 +236,7 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     g.keys = reinterpret_cast<unsigned long long*>(gb + cap * stride * 12);
     {
         TimingScope ts(h, s, 1);
-        e = tqfs::launch_general(a, g, ctas, s);
+        e = tqfs::launch_general(a, g, ctas, s, !relayout && !h->timing);
     }
     if (e != cudaSuccess) return cuda_fail(h, e, "general kernel launch");
     return TQFS_OK;

@@ -152,7 +152,8 @@ size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_st
     return static_cast<size_t>(ctas) * (*stride * 12 + *key_stride * 8);
 }
 
-cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s) {
+cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s,
+                           bool overlap) {
     if (a.rows <= 0 || a.vocab <= 0 || ctas <= 0) return cudaSuccess;
     const int smem = kFilterSmemBytes;
     static thread_local int configured = -1;  // the device whose attributes are set
@@ -166,9 +167,21 @@ cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int cta
         if (e != cudaSuccess) return e;
         configured = dev;
     }
-    if (a.dtype == TQFS_DTYPE_F32) general_kernel<0><<<ctas, kGenThreads, smem, s>>>(a, g);
-    else general_kernel<1><<<ctas, kGenThreads, smem, s>>>(a, g);
-    return cudaGetLastError();
+    // General rows read only the call's inputs, so with `overlap` the kernel
+    // may start while the kernel in front of it (the stream rows' finalize,
+    // which writes other rows) still runs.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    cfg.blockDim = dim3(kGenThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap ? 1 : 0;
+    if (a.dtype == TQFS_DTYPE_F32) return cudaLaunchKernelEx(&cfg, general_kernel<0>, a, g);
+    return cudaLaunchKernelEx(&cfg, general_kernel<1>, a, g);
 }
 
 }  // namespace tqfs

@@ -119,7 +119,8 @@ cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s,
 // behind the stream grid (programmatic serialization).
 cudaError_t launch_finalize(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool overlap);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
-cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s);
+cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s,
+                           bool overlap);
 cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab, long long ld,
                              const int32_t* hist, const int64_t* hist_off,
                              const tqfs_params* params, float* out, cudaStream_t s);

@@ -50,15 +50,18 @@ namespace tqfs {
 
 namespace {
 
-constexpr int kSW = 8;            // warps per CTA of the stream kernel
+constexpr int kSW = 11;           // warps per CTA of the stream kernel
+// Registers: 11 warps fit an SM at 168 registers a thread (3 warps on three
+// schedulers, 2 on the fourth, 16,128 of 16,384 registers each); the launch
+// bound of 384 threads makes the compiler hold to that.
+constexpr int kStreamBound = 384;
 constexpr int kST = kSW * 32;
 constexpr int kSlots = 16;        // float4 register slots per lane per chunk
 constexpr int kChunkLen = kSlots * 32 * 4;  // 2,048 ids per chunk
 constexpr int kListCap = 384;     // keys of a warp's candidate list
 constexpr int kListOff = 16384;   // per-warp shared memory: chunk buffers (+ exchange),
-constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins,
-constexpr int kSortOff = kBinsOff + 256 * 4;       // ranked keys of a finalised row
-constexpr int kWarpSmem = kSortOff + kStreamMaxK * 8;  // 21 KiB
+constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins
+constexpr int kWarpSmem = kBinsOff + 256 * 4;      // 20 KiB: 11 warps in 220 KiB
 constexpr int kMaxUnits = 32;                      // units per row (one lane each)
 constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
@@ -673,15 +676,16 @@ __device__ __forceinline__ void warp_rank_sort(const unsigned long long* src, in
     __syncwarp();
 }
 
-// The min(n, k) largest of the n (<= 128) distinct keys src[0..n), sorted
+// The min(n, k) largest of the n (<= 32 * R) distinct keys src[0..n), sorted
 // descending into dst (warp): each key's rank is the number of larger keys.
-__device__ __forceinline__ int warp_top_sorted(const unsigned long long* src, int n, int k,
-                                               unsigned long long* dst) {
+template <int R>
+__device__ __forceinline__ int warp_top_sorted_r(const unsigned long long* src, int n, int k,
+                                                 unsigned long long* dst) {
     const int lane = threadIdx.x & 31;
-    unsigned long long key[4];
-    int rank[4];
+    unsigned long long key[R];
+    int rank[R];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < R; ++r) {
         key[r] = r * 32 + lane < n ? src[r * 32 + lane] : ~0ull;
         rank[r] = 0;
     }
@@ -689,14 +693,21 @@ __device__ __forceinline__ int warp_top_sorted(const unsigned long long* src, in
     for (int j = 0; j < n; ++j) {
         const unsigned long long o = src[j];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) rank[r] += o > key[r] ? 1 : 0;
+        for (int r = 0; r < R; ++r) rank[r] += o > key[r] ? 1 : 0;
     }
     const int kk = n < k ? n : k;
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < R; ++r)
         if (r * 32 + lane < n && rank[r] < kk) dst[rank[r]] = key[r];
     __syncwarp();
     return kk;
+}
+
+__device__ __forceinline__ int warp_top_sorted(const unsigned long long* src, int n, int k,
+                                               unsigned long long* dst) {
+    if (n <= 32) return warp_top_sorted_r<1>(src, n, k, dst);
+    if (n <= 64) return warp_top_sorted_r<2>(src, n, k, dst);
+    return warp_top_sorted_r<4>(src, n, k, dst);
 }
 
 // A stop value no sum reaches (comparisons with NaN are false).
@@ -830,20 +841,19 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
 // filtered by the largest unit k-th value, then finish_sampled. In export
 // mode (a vocabulary shard) it writes the row's exact top-k (sampled) or
 // top-4 (greedy) keys with global ids to the row's record instead.
+// The caller passes what it loaded in one trip: the row's parameters, lane
+// u's unit list length m_raw and bound th_u (sampled rows), and whether the
+// call timed out.
 __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool greedy, int k,
-                                          unsigned long long* L, unsigned long long* S,
-                                          unsigned int* bins, int* counter) {
+                                          const tqfs_params& p, int m_raw, uint32_t th_u,
+                                          bool timed_out, unsigned long long* L,
+                                          unsigned long long* S, unsigned int* bins) {
     const int lane = threadIdx.x & 31;
     const int U = a.units;
     const size_t base = static_cast<size_t>(row) * U;
-    // Loads issued together: the lists' lengths and bounds, the row's knobs.
-    const int m_raw = (!greedy && lane < U) ? __ldcg(a.cand_n + base + lane) : 0;
-    const uint32_t th_u = (!greedy && lane < U) ? __ldcg(a.theta + base + lane) : 0u;
-    const tqfs_params p = greedy ? tqfs_params{} : a.params[row];
     unsigned long long* rec = a.export_rec != nullptr ? a.export_rec + static_cast<size_t>(row) * kShardRec : nullptr;
     const unsigned long long goff = static_cast<unsigned long long>(a.vocab_offset);
     int token = 0;
-    const bool timed_out = *reinterpret_cast<volatile uint32_t*>(a.err_word) == a.epoch;
     if (timed_out) {  // the units' lists may be missing: report and stop
         if (lane == 0) {
             if (rec != nullptr) {
@@ -1003,7 +1013,7 @@ __global__ void __launch_bounds__(kSW * 32) merge_kernel(MergeArgs m) {
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_diag) {
+__global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, int top4_diag) {
     constexpr int ES = Raw<DT>::kES;
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ int wcount[kSW];
@@ -1016,7 +1026,6 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
     float* xch = reinterpret_cast<float*>(wbase + 2 * Raw<DT>::kBuf);
     unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase + kListOff);
     unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + kBinsOff);
-    unsigned long long* S = reinterpret_cast<unsigned long long*>(wbase + kSortOff);
     if (lane == 0) {
         mbar_init(&wbar[warp][0], 1);
         mbar_init(&wbar[warp][1], 1);
@@ -1259,15 +1268,16 @@ __global__ void __launch_bounds__(kST, 1) stream_kernel(SampleArgs a, int top4_d
 // orders its reads after that grid's writes).
 __global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(SampleArgs a) {
     extern __shared__ __align__(16) unsigned char fdyn[];
-    __shared__ int fcount[kFinWarps];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     unsigned char* wb = fdyn + static_cast<size_t>(warp) * kFinWarpSmem;
     unsigned long long* L = reinterpret_cast<unsigned long long*>(wb);
     unsigned long long* S = L + kListCap;
     unsigned int* bins = reinterpret_cast<unsigned int*>(S + kStreamMaxK);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the general kernel
     const int row = static_cast<int>(blockIdx.x) * kFinWarps + warp;
     if (row >= a.rows) return;
+    // Everything the row needs from global memory, issued together.
     tqfs_params p{};
     if (!a.top4_only) p = a.params[row];  // no parameters in the top-4 mode
     long long hs = 0, he = 0, ws, wl;
@@ -1275,10 +1285,15 @@ __global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(SampleArgs a) 
         hs = a.hist_off[row];
         he = a.hist_off[row + 1];
     }
+    const size_t base = static_cast<size_t>(row) * a.units;
+    const bool lists = !a.top4_only && lane < a.units;
+    const int m_raw = lists ? __ldcg(a.cand_n + base + lane) : 0;
+    const uint32_t th_u = lists ? __ldcg(a.theta + base + lane) : 0u;
+    const bool timed_out = *reinterpret_cast<volatile uint32_t*>(a.err_word) == a.epoch;
     const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
     if (mode != kModeGreedy && mode != kModeStream) return;
-    (void)lane;
-    finalize_row(a, row, mode == kModeGreedy, static_cast<int>(p.top_k), L, S, bins, &fcount[warp]);
+    finalize_row(a, row, mode == kModeGreedy, static_cast<int>(p.top_k), p, mode == kModeGreedy ? 0 : m_raw,
+                 mode == kModeGreedy ? 0u : th_u, timed_out, L, S, bins);
 }
 
 // Buckets the penalty window of every stream-sampled row by chunk and counts
