@@ -65,7 +65,7 @@ constexpr int kWarpSmem = kBinsOff + 256 * 4;      // 20 KiB: 11 warps in 220 Ki
 constexpr int kMaxUnits = 32;                      // units per row (one lane each)
 constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
-constexpr int kWinWarps = 8;      // warps of the window kernel
+constexpr int kWinWarps = 16;     // warps of the window kernel
 constexpr int kFinWarps = 8;      // warps (rows) per CTA of the finalize kernel
 constexpr int kFinWarpSmem = kListCap * 8 + kStreamMaxK * 8 + 256 * 4;
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
