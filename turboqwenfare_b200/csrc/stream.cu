@@ -1227,8 +1227,11 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                                  : chunk_select<false>(vals, n_here, base_id, k, L + n, &wcount[warp]);
                     n += c;
                 }
-                // ---- 5. keep L short; with k keys it defines the unit's k-th
-                if (full ? n >= k : n > kListCap - kChunkCap) {
+                // ---- 5. keep L short; with k keys it defines the unit's k-th.
+                // Cutting back to k once the list doubles keeps th close to the
+                // k-th of everything seen, so later chunks append few ids.
+                const int cut = min(max(2 * k, 32), kListCap - kChunkCap);
+                if (full ? n >= k : n >= cut) {
                     const unsigned long long kth = warp_keep_top(L, &n, k, bins);
                     th_ord = static_cast<uint32_t>(kth >> 32);
                     sel = n >= k && th_ord != 0u;  // a NaN k-th admits every number
