@@ -66,7 +66,7 @@ constexpr int kMaxUnits = 32;                      // units per row (one lane ea
 constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
 constexpr int kWinWarps = 16;     // warps of the window kernel
-constexpr int kFinWarps = 8;      // warps (rows) per CTA of the finalize kernel
+constexpr int kFinWarps = 4;      // warps (rows) per CTA of the finalize kernel
 constexpr int kFinWarpSmem = kListCap * 8 + kStreamMaxK * 8 + 256 * 4;
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
 
