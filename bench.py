@@ -12,7 +12,7 @@ batch resident in HBM. Inputs rotate over enough buffers to exceed 2x L2.
 Multi-GPU runs shard rows (each rank owns its own 256-row block; no
 collective on the data path): weak scaling.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c1x256|c1|c0|c2|c4]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c1x256|c1|c0|c2|c3|c4]
   python bench.py --impl reference ...   # the reference CPU sampler (oracle port)
 """
 from __future__ import annotations
@@ -411,6 +411,103 @@ def run_vocab_sharded(args):
         dist.destroy_process_group()
 
 
+def run_mtp(args):
+    """Configuration 3: MTP verify of 32 sequences x (3 drafts + bonus) per
+    call (tqfs_mtp_verify). The metric counts the target rows a call verifies
+    (seqs x (L + 1)); rows shard across ranks with no collective."""
+    import ctypes
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import turboqwenfare_b200._native as N
+    from turboqwenfare_b200 import workloads as W
+    from turboqwenfare_b200.sampler import params_tensor
+    m = W.mtp_config(seed=args.seed + 7919 * rank)
+    S, L, V = m.seqs, m.draft_len, m.target.shape[-1]
+    rows = S * (L + 1)
+    tgt = torch.from_numpy(m.target).to(dev)
+    dft = torch.from_numpy(m.draft).to(dev)
+    drafts = torch.from_numpy(m.drafts).to(dev)
+    params = params_tensor(m.params, S, dev)
+    uni = torch.from_numpy(m.uniforms).to(dev)
+    acc = torch.empty(S, dtype=torch.int32, device=dev)
+    tok = torch.empty(S, dtype=torch.int32, device=dev)
+    mask = torch.empty((S, L), dtype=torch.uint8, device=dev)
+    st = torch.empty(S, dtype=torch.int32, device=dev)
+    h = N.Handle(local)
+    Lb = N.lib()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+
+    def call(t_ptr, d_ptr):
+        r = Lb.tqfs_mtp_verify(h.ptr, t_ptr, d_ptr, N.DTYPE_F32, S, L, V, V, drafts.data_ptr(),
+                               params.data_ptr(), uni.data_ptr(), acc.data_ptr(), tok.data_ptr(),
+                               mask.data_ptr(), st.data_ptr(), sp)
+        if r != 0:
+            h.check(r)
+
+    for _ in range(max(args.warmup, 3)):
+        call(tgt.data_ptr(), dft.data_ptr())
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call(tgt.data_ptr(), dft.data_ptr())
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clk = clocks.stop()
+    ms_per_step = ms / args.steps
+    # e2e: the rows copied from pinned host memory each call, the results back
+    th = torch.from_numpy(m.target).pin_memory()
+    dh = torch.from_numpy(m.draft).pin_memory()
+    out_h = torch.empty(S, dtype=torch.int32, pin_memory=True)
+    torch.cuda.synchronize()
+    e2 = max(3, args.e2e_steps)
+    t0 = time.perf_counter()
+    for _ in range(e2):
+        tgt.copy_(th, non_blocking=True)
+        dft.copy_(dh, non_blocking=True)
+        call(tgt.data_ptr(), dft.data_ptr())
+        out_h.copy_(tok, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        done, t1 = 0, time.perf_counter()
+        while time.perf_counter() - t1 < 10.0:
+            O.mtp_verify(m.target, m.draft, m.drafts.astype(np.uint32), m.params, m.uniforms)
+            done += rows
+        dt = time.perf_counter() - t1
+        base = {"value": done / dt, "unit": "rows/s", "cores": 1, "kind": "port",
+                "sample": f"{done // rows} oracle verify calls of configuration 3 in {dt:.1f}s"}
+    line = {
+        "metric": "verified target rows/sec at V=151,936", "value": round(rows * world * args.steps / (ms / 1000.0), 1),
+        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "c3", "seqs_per_gpu": S, "draft_len": L, "vocab": V, "temperature": 0.8,
+                   "top_p": 0.9, "l2": "inputs resident (78 MB), no flush"},
+        "cpu_baseline": base,
+        "e2e": {"value": round(rows * world / e2e_s, 1), "unit": "rows/s",
+                "h2d_bytes_per_step": int(m.target.nbytes + m.draft.nbytes), "d2h_bytes_per_step": 4 * S},
+        "gpu_launches": args.steps * 2, "clocks": clk,  # the row kernel and the decide kernel
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    import torch.distributed as dist
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
 def _free_port():
     import socket
     with socket.socket() as sk:
@@ -424,6 +521,8 @@ def main():
         run_reference(args)
     elif args.vocab_shard:
         run_vocab_sharded(args)
+    elif args.workload == "c3":
+        run_mtp(args)
     else:
         run_ours(args)
 

@@ -526,18 +526,19 @@ int tqfs_mtp_verify(tqfs_handle* h, const void* target_dev, const void* draft_de
         return fail(h, TQFS_ERR_INVALID_ARG, "NULL argument");
     int st = ensure_current(h);
     if (st != TQFS_OK) return st;
-    const int ctas = seqs < 64 ? seqs : 64;
-    size_t stride = 0, key_stride = 0;
-    const size_t bytes = tqfs::mtp_scratch_bytes(vocab, ctas, &stride, &key_stride);
+    // Rows run in parallel, one CTA each (up to one per SM), over batches of
+    // up to 64 sequences (each batch keeps 2 * L dense q rows per sequence).
+    const int batch = seqs < 64 ? seqs : 64;
+    const int jobs = batch * (2 * draft_len + 1);
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device) != cudaSuccess || sms <= 0)
+        sms = 148;
+    const int ctas = jobs < sms ? jobs : sms;
+    const size_t bytes = tqfs::mtp_layout(vocab, ctas, batch, draft_len, nullptr, nullptr);
     cudaError_t e = h->mtp.reserve(bytes);
     if (e != cudaSuccess) return cuda_fail(h, e, "MTP scratch allocation");
     tqfs::MtpScratch g;
-    g.stride = stride;
-    g.key_stride = key_stride;
-    unsigned char* b = static_cast<unsigned char*>(h->mtp.ptr);
-    g.work = reinterpret_cast<float*>(b);
-    g.e = reinterpret_cast<float*>(b + static_cast<size_t>(ctas) * 2 * stride * 4);
-    g.keys = reinterpret_cast<unsigned long long*>(b + static_cast<size_t>(ctas) * 2 * stride * 8);
+    tqfs::mtp_layout(vocab, ctas, batch, draft_len, h->mtp.ptr, &g);
     tqfs::MtpArgs m;
     m.target = target_dev;
     m.draft = draft_dev;
@@ -556,7 +557,7 @@ int tqfs_mtp_verify(tqfs_handle* h, const void* target_dev, const void* draft_de
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     {
         TimingScope ts(h, s, 3);
-        e = tqfs::launch_mtp(m, g, ctas, s);
+        e = tqfs::launch_mtp(m, g, ctas, batch, s);
     }
     return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "MTP verify launch");
 }

@@ -93,8 +93,10 @@ struct MtpScratch {
     float* work;               // logits, then candidate tokens
     float* e;                  // exponentials
     unsigned long long* keys;  // probability keys
-    size_t stride;             // floats per workspace in work / e
+    size_t stride;             // floats per workspace in work / e (and per q row)
     size_t key_stride;         // keys per list (a power of two >= vocab)
+    float* q;                  // per batch: dense q of target rows < L, then draft rows
+    int32_t* pick;             // per batch: target rows' draw with u_L (greedy: argmax)
 };
 
 struct Plan {
@@ -125,8 +127,10 @@ cudaError_t launch_penalties(const void* logits, int dtype, int rows, int vocab,
                              const int32_t* hist, const int64_t* hist_off,
                              const tqfs_params* params, float* out, cudaStream_t s);
 cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s);
-size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
-cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s);
+// MTP scratch for `ctas` row CTAs and batches of `batch` sequences: returns
+// its bytes, and with a base, lays it out in *g.
+size_t mtp_layout(int vocab, int ctas, int batch, int draft_len, void* base, MtpScratch* g);
+cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, int batch, cudaStream_t s);
 cudaError_t launch_fill_empty(int rows, int32_t* out_token, int32_t* out_status,
                               tqfs_candidate* out_top4, cudaStream_t s);
 

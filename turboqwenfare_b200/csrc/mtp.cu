@@ -18,9 +18,13 @@
 // Penalties are not part of verification; a sequence whose parameters carry
 // an active penalty gets status TQFS_ROW_ERR_UNSUPPORTED.
 //
-// One 512-thread CTA per sequence, persistent over the sequences. Each row
-// runs the exact filter chain of filter.cuh; the target and draft rows of a
-// position sit in two workspaces of the CTA.
+// Two kernels per batch of sequences. mtp_rows_kernel runs every row at once
+// (one 512-thread CTA per row, persistent over the rows): the exact filter
+// chain of filter.cuh on each target and draft row, leaving per row the dense
+// q (every id's post-filter probability) and, for target rows, the sampler's
+// draw with u_L (greedy sequences: the target rows' argmax instead).
+// mtp_decide_kernel then takes each sequence's decisions, residual draw and
+// bonus token from those (one CTA per sequence).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -41,12 +45,11 @@ struct Workspace {
     unsigned long long* K;
 };
 
-__device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta, int which) {
+__device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta) {
     Workspace w;
-    const size_t slot = static_cast<size_t>(cta) * 2 + which;
-    w.W = g.work + slot * g.stride;
-    w.E = g.e + slot * g.stride;
-    w.K = g.keys + slot * g.key_stride;
+    w.W = g.work + static_cast<size_t>(cta) * g.stride;
+    w.E = g.e + static_cast<size_t>(cta) * g.stride;
+    w.K = g.keys + static_cast<size_t>(cta) * g.key_stride;
     return w;
 }
 
@@ -68,34 +71,23 @@ __device__ int row_argmax(const MtpArgs& m, const void* base, size_t row,
     return best ? static_cast<int>(key_token(best)) : 0;
 }
 
-// q(x) of a filter_row result (see the file comment), in shared *out.
-__device__ void q_of(const Workspace& w, const FilterOut& fo, int x, int vocab, float* out) {
-    if (threadIdx.x == 0) *out = 0.0f;
+// q of a filter_row result for every id, dense in Q: zero except the kept
+// ids (a point mass on the first kept id when the draw total is not a
+// positive number).
+__device__ void q_dense(const unsigned long long* K, const FilterOut& fo, int vocab, float* Q) {
+    for (int i = threadIdx.x; i < vocab; i += kMT) Q[i] = 0.0f;
     __syncthreads();
-    if (x >= 0 && x < vocab) {
-        if (!(isfinite(fo.total2) && fo.total2 > 0.0f)) {
-            if (threadIdx.x == 0 && static_cast<int>(key_token(w.K[0])) == x) *out = 1.0f;
-        } else {
-            for (int i = threadIdx.x; i < fo.keep; i += kMT)
-                if (static_cast<int>(key_token(w.K[i])) == x) *out = __fdiv_rn(key_value(w.K[i]), fo.total2);
-        }
+    if (!(isfinite(fo.total2) && fo.total2 > 0.0f)) {
+        if (threadIdx.x == 0 && fo.keep > 0) Q[key_token(K[0])] = 1.0f;
+    } else {
+        for (int i = threadIdx.x; i < fo.keep; i += kMT)
+            Q[key_token(K[i])] = __fdiv_rn(key_value(K[i]), fo.total2);
     }
     __syncthreads();
 }
 
-// q of a filter_row result for every id, dense in w.W (free once filter_row
-// has run): zero except the kept ids.
-__device__ void q_dense(const Workspace& w, const FilterOut& fo, int vocab) {
-    float* Q = w.W;
-    for (int i = threadIdx.x; i < vocab; i += kMT) Q[i] = 0.0f;
-    __syncthreads();
-    if (!(isfinite(fo.total2) && fo.total2 > 0.0f)) {
-        if (threadIdx.x == 0 && fo.keep > 0) Q[key_token(w.K[0])] = 1.0f;
-    } else {
-        for (int i = threadIdx.x; i < fo.keep; i += kMT)
-            Q[key_token(w.K[i])] = __fdiv_rn(key_value(w.K[i]), fo.total2);
-    }
-    __syncthreads();
+__device__ __forceinline__ bool penalised(const tqfs_params& p) {
+    return !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f && p.presence_penalty == 0.0f);
 }
 
 // An id's residual max(0, q_target - q_draft) as a multiple of 2^-62.
@@ -152,26 +144,61 @@ __device__ int residual_token(const float* QT, const float* QD, int vocab, float
     return r;
 }
 
+// Phase 1: rows s0 .. s0 + ns - 1 of every kind. Job j < ns * (L + 1) is
+// target row (j / (L + 1), j % (L + 1)); the rest are draft rows.
 template <int DT>
-__global__ void __launch_bounds__(kMT, 1) mtp_kernel(MtpArgs m, MtpScratch g) {
+__global__ void __launch_bounds__(kMT, 1) mtp_rows_kernel(MtpArgs m, MtpScratch g, int s0, int ns) {
     __shared__ float red[kMT / 32];
     __shared__ unsigned long long redk[kMT / 32];
-    __shared__ FilterOut ft, fd;
-    __shared__ float qv[2];
+    __shared__ FilterOut fo;
     __shared__ int sh[4];
     extern __shared__ __align__(16) unsigned char dyn_smem[];
     FastShared* fs = reinterpret_cast<FastShared*>(dyn_smem);
     unsigned long long* sk = reinterpret_cast<unsigned long long*>(dyn_smem + kFastSharedBytes);
-    const int tid = threadIdx.x;
-    const Workspace A = workspace(g, blockIdx.x, 0);
-    const Workspace B = workspace(g, blockIdx.x, 1);
-    const int L = m.draft_len;
-    for (int s = blockIdx.x; s < m.seqs; s += gridDim.x) {
+    const Workspace A = workspace(g, blockIdx.x);
+    const int L = m.draft_len, T = L + 1;
+    const int njobs = ns * (T + L);
+    for (int job = blockIdx.x; job < njobs; job += gridDim.x) {
+        const bool tgt = job < ns * T;
+        const int sl = tgt ? job / T : (job - ns * T) / L;
+        const int j = tgt ? job % T : (job - ns * T) % L;
+        const int s = s0 + sl;
         const tqfs_params p = m.params[s];
-        const size_t trow0 = static_cast<size_t>(s) * (L + 1);
-        const size_t drow0 = static_cast<size_t>(s) * L;
-        const float* us = m.uniforms + static_cast<size_t>(s) * (L + 1);
-        if (!(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f && p.presence_penalty == 0.0f)) {
+        if (penalised(p)) continue;  // refused in phase 2
+        if (p.temperature == 0.0f) {  // greedy: verify_pair needs the target argmax
+            if (tgt) {
+                const int t = row_argmax<DT>(m, m.target, static_cast<size_t>(s) * T + j, redk);
+                if (threadIdx.x == 0) g.pick[static_cast<size_t>(sl) * T + j] = t;
+            }
+            continue;
+        }
+        const size_t row = tgt ? static_cast<size_t>(s) * T + j : static_cast<size_t>(s) * L + j;
+        load_row<DT>(m, tgt ? m.target : m.draft, row, A.W);
+        filter_row(A.W, A.E, A.K, m.vocab, p, red, &fo, fs, sk);
+        if (tgt) {  // the sampler's draw with u_L: the bonus token, or the zero-residual fallback
+            const float uL = m.uniforms[static_cast<size_t>(s) * T + L];
+            const int t = draw_row<kMT>(A.K, fo, uL, fs, &sh[0]);
+            if (threadIdx.x == 0) g.pick[static_cast<size_t>(sl) * T + j] = t;
+        }
+        if (!tgt || j < L) {
+            const size_t slot = tgt ? static_cast<size_t>(sl) * L + j
+                                    : static_cast<size_t>(ns) * L + static_cast<size_t>(sl) * L + j;
+            q_dense(A.K, fo, m.vocab, g.q + slot * g.stride);
+        }
+        __syncthreads();
+    }
+}
+
+// Phase 2: one CTA per sequence of the batch.
+__global__ void __launch_bounds__(kMT) mtp_decide_kernel(MtpArgs m, MtpScratch g, int s0, int ns) {
+    __shared__ unsigned long long redk[kMT / 32];
+    __shared__ int sh[4];
+    const int tid = threadIdx.x;
+    const int L = m.draft_len, T = L + 1;
+    for (int sl = blockIdx.x; sl < ns; sl += gridDim.x) {
+        const int s = s0 + sl;
+        const tqfs_params p = m.params[s];
+        if (penalised(p)) {
             if (tid == 0) {
                 m.out_accepted[s] = -1;
                 m.out_token[s] = -1;
@@ -180,45 +207,36 @@ __global__ void __launch_bounds__(kMT, 1) mtp_kernel(MtpArgs m, MtpScratch g) {
             continue;
         }
         const bool greedy = p.temperature == 0.0f;
+        const float* us = m.uniforms + static_cast<size_t>(s) * T;
+        const int* pick = g.pick + static_cast<size_t>(sl) * T;
         int accepted = -1, token = 0;
         for (int j = 0; j < L; ++j) {
-            const int x = m.drafts[drow0 + j];
+            const int x = m.drafts[static_cast<size_t>(s) * L + j];
             bool ok;
             if (greedy) {
                 // verify_pair (src/runtime/mtp.rs:98-104)
-                const int t = row_argmax<DT>(m, m.target, trow0 + j, redk);
-                ok = t == x;
+                ok = pick[j] == x;
                 if (!ok && accepted < 0) {
                     accepted = j;
-                    token = t;
+                    token = pick[j];
                 }
             } else {
-                load_row<DT>(m, m.target, trow0 + j, A.W);
-                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft, fs, sk);
-                load_row<DT>(m, m.draft, drow0 + j, B.W);
-                filter_row(B.W, B.E, B.K, m.vocab, p, red, &fd, fs, sk);
-                q_of(A, ft, x, m.vocab, &qv[0]);
-                q_of(B, fd, x, m.vocab, &qv[1]);
-                ok = __fmul_rn(us[j], qv[1]) < qv[0];
+                const float* QT = g.q + (static_cast<size_t>(sl) * L + j) * g.stride;
+                const float* QD = g.q + (static_cast<size_t>(ns) * L + static_cast<size_t>(sl) * L + j) * g.stride;
+                const bool in = x >= 0 && x < m.vocab;
+                const float qt = in ? QT[x] : 0.0f, qd = in ? QD[x] : 0.0f;
+                ok = __fmul_rn(us[j], qd) < qt;
                 if (!ok && accepted < 0) {
                     accepted = j;
-                    q_dense(A, ft, m.vocab);
-                    q_dense(B, fd, m.vocab);
-                    token = residual_token(A.W, B.W, m.vocab, us[L], redk, &sh[0]);
-                    if (token < 0) token = draw_row<kMT>(A.K, ft, us[L], fs, &sh[0]);
+                    token = residual_token(QT, QD, m.vocab, us[L], redk, &sh[0]);
+                    if (token < 0) token = pick[j];
                 }
             }
-            if (tid == 0 && m.out_mask != nullptr) m.out_mask[drow0 + j] = ok ? 1 : 0;
+            if (tid == 0 && m.out_mask != nullptr) m.out_mask[static_cast<size_t>(s) * L + j] = ok ? 1 : 0;
         }
         if (accepted < 0) {  // every draft accepted: the bonus token from row L
             accepted = L;
-            if (greedy) {
-                token = row_argmax<DT>(m, m.target, trow0 + L, redk);
-            } else {
-                load_row<DT>(m, m.target, trow0 + L, A.W);
-                filter_row(A.W, A.E, A.K, m.vocab, p, red, &ft, fs, sk);
-                token = draw_row<kMT>(A.K, ft, us[L], fs, &sh[0]);
-            }
+            token = pick[L];
         }
         if (tid == 0) {
             m.out_accepted[s] = accepted;
@@ -231,17 +249,31 @@ __global__ void __launch_bounds__(kMT, 1) mtp_kernel(MtpArgs m, MtpScratch g) {
 
 }  // namespace
 
-size_t mtp_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride) {
+size_t mtp_layout(int vocab, int ctas, int batch, int draft_len, void* base, MtpScratch* g) {
     const size_t v = static_cast<size_t>(vocab > 0 ? vocab : 1);
-    *stride = (v + 63) & ~static_cast<size_t>(63);
+    const size_t stride = (v + 63) & ~static_cast<size_t>(63);
     size_t p2 = 1;
     while (p2 < v) p2 <<= 1;
-    *key_stride = p2;
-    // per CTA two workspaces: W and E (stride floats each) and K (p2 keys)
-    return static_cast<size_t>(ctas) * 2 * (*stride * 8 + *key_stride * 8);
+    const size_t c = static_cast<size_t>(ctas), L = static_cast<size_t>(draft_len);
+    // per CTA a workspace (W and E: stride floats each; K: p2 keys), per
+    // batch 2 * batch * L dense q rows and batch * (L + 1) picks
+    const size_t work = c * stride * 4, e = c * stride * 4, keys = c * p2 * 8;
+    const size_t q = 2 * static_cast<size_t>(batch) * L * stride * 4;
+    const size_t pick = (static_cast<size_t>(batch) * (L + 1) * 4 + 255) & ~static_cast<size_t>(255);
+    if (base != nullptr) {
+        unsigned char* b = static_cast<unsigned char*>(base);
+        g->stride = stride;
+        g->key_stride = p2;
+        g->work = reinterpret_cast<float*>(b);
+        g->e = reinterpret_cast<float*>(b + work);
+        g->keys = reinterpret_cast<unsigned long long*>(b + work + e);
+        g->q = reinterpret_cast<float*>(b + work + e + keys);
+        g->pick = reinterpret_cast<int32_t*>(b + work + e + keys + q);
+    }
+    return work + e + keys + q + pick;
 }
 
-cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStream_t s) {
+cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, int batch, cudaStream_t s) {
     if (m.seqs <= 0 || ctas <= 0) return cudaSuccess;
     const int smem = kFilterSmemBytes;
     static thread_local int configured = -1;  // the device whose attributes are set
@@ -249,14 +281,24 @@ cudaError_t launch_mtp(const MtpArgs& m, const MtpScratch& g, int ctas, cudaStre
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (configured != dev) {
-        e = cudaFuncSetAttribute(mtp_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mtp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(mtp_rows_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mtp_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured = dev;
     }
-    if (m.dtype == TQFS_DTYPE_F32) mtp_kernel<0><<<ctas, kMT, smem, s>>>(m, g);
-    else mtp_kernel<1><<<ctas, kMT, smem, s>>>(m, g);
-    return cudaGetLastError();
+    for (int s0 = 0; s0 < m.seqs; s0 += batch) {
+        const int ns = m.seqs - s0 < batch ? m.seqs - s0 : batch;
+        const int jobs = ns * (2 * m.draft_len + 1);
+        const int grid = jobs < ctas ? jobs : ctas;
+        if (m.dtype == TQFS_DTYPE_F32) mtp_rows_kernel<0><<<grid, kMT, smem, s>>>(m, g, s0, ns);
+        else mtp_rows_kernel<1><<<grid, kMT, smem, s>>>(m, g, s0, ns);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        mtp_decide_kernel<<<ns, kMT, 0, s>>>(m, g, s0, ns);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace tqfs
