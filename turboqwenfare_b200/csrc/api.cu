@@ -206,7 +206,9 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
     if (a.top4_only) return TQFS_OK;
     // Rows the stream kernel does not own run the general kernel.
-    const int ctas = a.rows < 64 ? a.rows : 64;
+    // General rows spread evenly over up to 96 CTAs (about 3.9 MB of scratch
+    // each at V = 151,936).
+    const int ctas = a.rows < 96 ? a.rows : 96;
     size_t stride = 0, key_stride = 0;
     const size_t bytes = tqfs::general_scratch_bytes(a.vocab, ctas, &stride, &key_stride);
     const bool relayout = h->general_layout[0] != stride || h->general_layout[1] != key_stride ||

@@ -57,21 +57,32 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
     float* E = g.e + static_cast<size_t>(blockIdx.x) * g.stride;
     unsigned long long* K = g.keys + static_cast<size_t>(blockIdx.x) * g.key_stride;
 
-    // This CTA's general rows (rows blockIdx.x + gridDim.x * i), found by all
-    // threads at once and listed in shared memory.
+    // Every CTA lists the general rows of each block of kGenThreads rows in
+    // row order (a ballot per warp); the i-th general row of the call goes to
+    // CTA i % gridDim, so the rows spread evenly however they are placed.
     __shared__ int list[kGenThreads];
-    __shared__ int nlist;
-    for (int r0 = blockIdx.x; r0 < a.rows; r0 += gridDim.x * kGenThreads) {
-    if (tid == 0) nlist = 0;
-    __syncthreads();
+    __shared__ int wcnt[kGenThreads / 32];
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = static_cast<int>(gridDim.x);
+    int carry = 0;  // general rows in the blocks before this one
+    for (int r0 = 0; r0 < a.rows; r0 += kGenThreads) {
     {
-        const int rr = r0 + gridDim.x * tid;
-        if (rr < a.rows && is_general(a, rr, a.params[rr])) list[atomicAdd(&nlist, 1)] = rr;
+        const int rr = r0 + tid;
+        const bool gen = rr < a.rows && is_general(a, rr, a.params[rr]);
+        const unsigned bal = __ballot_sync(0xFFFFFFFFu, gen);
+        if (lane == 0) wcnt[warp] = __popc(bal);
+        __syncthreads();
+        int off = 0;
+        for (int w = 0; w < warp; ++w) off += wcnt[w];
+        if (gen) list[off + __popc(bal & ((1u << lane) - 1u))] = rr;
     }
+    int nl = 0;
+    for (int w = 0; w < kGenThreads / 32; ++w) nl += wcnt[w];
     __syncthreads();
-    const int nl = nlist;
+    const int first = ((static_cast<int>(blockIdx.x) - carry) % G + G) % G;
+    carry += nl;
 #pragma unroll 1
-    for (int li = 0; li < nl; ++li) {
+    for (int li = first; li < nl; li += G) {
         const int row = list[li];
         const tqfs_params p = a.params[row];
         const size_t base = static_cast<size_t>(row) * a.ld;
