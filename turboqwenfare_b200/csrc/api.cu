@@ -56,6 +56,7 @@ struct tqfs_handle {
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
     DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
+    DeviceBuffer row_th;       // per-row bounds shared by a row's units, tagged by call
     DeviceBuffer mtp;          // MTP verify workspaces
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
@@ -167,7 +168,13 @@ int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::Sampl
         if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     }
     if (++h->epoch == 0u) h->epoch = 1u;
+    if (h->row_th.bytes < static_cast<size_t>(rows) * 8) {  // new memory starts at zero
+        e = h->row_th.reserve(static_cast<size_t>(rows) * 8);
+        if (e == cudaSuccess) e = cudaMemset(h->row_th.ptr, 0, h->row_th.bytes);
+        if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
+    }
     a.err_word = static_cast<uint32_t*>(h->err_word.ptr);
+    a.row_th = static_cast<unsigned long long*>(h->row_th.ptr);
     a.epoch = h->epoch;
     return TQFS_OK;
 }
@@ -307,6 +314,7 @@ int tqfs_destroy(tqfs_handle* h) {
     h->scratch.release();
     h->general.release();
     h->err_word.release();
+    h->row_th.release();
     h->mtp.release();
     h->shard_send.release();
     h->shard_recv.release();

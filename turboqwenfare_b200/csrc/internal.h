@@ -38,6 +38,7 @@ struct SampleArgs {
     int unit_len;              // chunks per unit (a warp's run of one row)
     int units;                 // units per row
     uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
+    unsigned long long* row_th;  // rows: (epoch << 32) | the largest unit bound published
     uint32_t epoch;            // this call's number (never 0)
     int vec_ok;                // rows start on 16-byte boundaries
     int vocab_route;           // vocabulary the routing compares top_k with

@@ -34,11 +34,13 @@ constexpr size_t kStaticBytes = static_cast<size_t>(48) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
 static __device__ uint32_t g_static_err;  // zero at load; see SampleArgs::epoch
 constexpr int kStaticRows = 4096;
+static __device__ unsigned long long g_static_row_th[kStaticRows];  // zero at load; tagged by epoch
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
 void* g_err_addr[kMaxDevices] = {};
+void* g_row_th_addr[kMaxDevices] = {};
 uint32_t g_epoch[kMaxDevices] = {};
 
 // Rows the stream kernel does not own (general rows) keep this status.
@@ -60,6 +62,9 @@ cudaError_t static_scratch(int device, void** out, uint32_t** err, uint32_t* epo
         void* eptr = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e == cudaSuccess) e = cudaGetSymbolAddress(&eptr, g_static_err);
+        void* rptr = nullptr;
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&rptr, g_static_row_th);
+        g_row_th_addr[device] = rptr;
         if (e != cudaSuccess) return e;
         g_scratch_addr[device] = ptr;
         g_err_addr[device] = eptr;
@@ -115,6 +120,7 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     a.out_status = out_status_dev;
     stream_scratch(rows, plan, base, &a);
     a.err_word = err;
+    a.row_th = static_cast<unsigned long long*>(g_row_th_addr[device]);
     a.epoch = epoch;
     const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = (reinterpret_cast<uintptr_t>(logits_dev) & 15u) == 0 &&

@@ -621,10 +621,13 @@ __device__ __forceinline__ int scan_slots(const void* vals, unsigned mask, int n
 // k; theta becomes the unit's th. Appends go to out[0..room) at positions
 // from a warp scan of the lanes' counts. Returns the number appended; -1 when
 // the chunk needs the full selection (more ids than room, or fewer than k
-// reach theta).
+// reach theta). With incl_sel (a bound another unit of the row published,
+// at or below the row's k-th but not this unit's own) the test is v >= th:
+// an id equal to it may still precede that unit's k-th.
 template <bool F32>
 __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel, float& th, int k,
-                                          int base_id, unsigned long long* out, int room) {
+                                          int base_id, unsigned long long* out, int room,
+                                          bool incl_sel = false) {
     const int lane = threadIdx.x & 31;
     float sm[kSlots];
     slot_maxima<F32>(vals, n_here, lane, sm);
@@ -647,16 +650,17 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
         }
         if (!(thr > -INFINITY)) return -1;  // too few numbers: select in full
     }
+    const bool incl = !sel || incl_sel;
     unsigned mask = 0u;
 #pragma unroll
     for (int j = 0; j < kSlots; ++j)
-        mask |= static_cast<unsigned>(sel ? sm[j] > thr : sm[j] >= thr) << j;
+        mask |= static_cast<unsigned>(incl ? sm[j] >= thr : sm[j] > thr) << j;
     if (!__any_sync(0xFFFFFFFFu, mask != 0u)) return 0;
-    const int mine = mask ? scan_slots<F32, false>(vals, mask, n_here, thr, !sel, base_id, out, 0, room) : 0;
+    const int mine = mask ? scan_slots<F32, false>(vals, mask, n_here, thr, incl, base_id, out, 0, room) : 0;
     const int excl = warp_excl_scan(mine, lane);
     const int total = __shfl_sync(0xFFFFFFFFu, excl + mine, 31);
     if (total > room || (!sel && total < k)) return -1;
-    if (mask) scan_slots<F32, true>(vals, mask, n_here, thr, !sel, base_id, out, excl, room);
+    if (mask) scan_slots<F32, true>(vals, mask, n_here, thr, incl, base_id, out, excl, room);
     __syncwarp();
     if (!sel) th = thr;
     return total;
@@ -1211,10 +1215,22 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                 // ---- 3. the chunk's candidates, appended to L -------------
                 // The unit's first chunk keeps the ids at or above its theta
                 // (k of them reach it); later chunks keep what beats th.
+                // A row's units share their bounds: the largest k-th value
+                // any unit of the row has published this call (each is at or
+                // below the row's k-th) filters with >= when it beats th.
                 const int room = kListCap - n;
                 float th = sel ? from_order32(th_ord) : 0.0f;
-                int c = vals_f32 ? unit_chunk<true>(vals, n_here, sel, th, k, base_id, L + n, room)
-                                 : unit_chunk<false>(vals, n_here, sel, th, k, base_id, L + n, room);
+                bool incl_sel = false;
+                if (sel && a.row_th != nullptr) {
+                    const unsigned long long rb = __ldcg(a.row_th + cur.row);
+                    const uint32_t fo = (rb >> 32) == a.epoch ? static_cast<uint32_t>(rb) : 0u;
+                    if (fo > th_ord) {
+                        th = from_order32(fo);
+                        incl_sel = true;
+                    }
+                }
+                int c = vals_f32 ? unit_chunk<true>(vals, n_here, sel, th, k, base_id, L + n, room, incl_sel)
+                                 : unit_chunk<false>(vals, n_here, sel, th, k, base_id, L + n, room, incl_sel);
                 bool full = !sel;  // the first chunk's list defines the exact k-th
                 if (c >= 0) {
                     n += c;
@@ -1235,6 +1251,8 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                     const unsigned long long kth = warp_keep_top(L, &n, k, bins);
                     th_ord = static_cast<uint32_t>(kth >> 32);
                     sel = n >= k && th_ord != 0u;  // a NaN k-th admits every number
+                    if (sel && lane == 0 && a.row_th != nullptr)
+                        atomicMax(a.row_th + cur.row, (static_cast<unsigned long long>(a.epoch) << 32) | th_ord);
                 }
                 // ---- 6. unit end: its exact top-k and its k-th value -------
                 if (cur.last) {
