@@ -1127,6 +1127,9 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
         w2 = info_word(a, p2, same_unit(p2, nn), lane);
         uint32_t enn[4];
         load_entries(nxt, enn);
+        // The row's shared bound (used below), loaded before the copy wait.
+        const unsigned long long rb =
+            (sel && a.row_th != nullptr && cur.mode == kModeStream) ? __ldcg(a.row_th + cur.row) : 0ull;
         if (!failed) {
             const bool ok = mbar_wait_bounded(&wbar[warp][b], (parity >> b) & 1u, kWaitBudgetNs);
             parity ^= 1u << b;
@@ -1221,8 +1224,7 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                 const int room = kListCap - n;
                 float th = sel ? from_order32(th_ord) : 0.0f;
                 bool incl_sel = false;
-                if (sel && a.row_th != nullptr) {
-                    const unsigned long long rb = __ldcg(a.row_th + cur.row);
+                if (sel) {
                     const uint32_t fo = (rb >> 32) == a.epoch ? static_cast<uint32_t>(rb) : 0u;
                     if (fo > th_ord) {
                         th = from_order32(fo);
