@@ -12,7 +12,14 @@ batch resident in HBM. Inputs rotate over enough buffers to exceed 2x L2.
 Multi-GPU runs shard rows (each rank owns its own 256-row block; no
 collective on the data path): weak scaling.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c1x256|c1|c0|c2|c3|c4]
+The step is timed in passes of exactly K steps, repeated until about 0.4 s of
+device time has run; the median pass is reported. The same line carries
+configurations 2 and 3 (`other_workloads`), and with N > 1 GPUs the
+vocabulary-split configuration 4 (`vocab_shard`: NCCL all-gather of per-shard
+top-50 records, with the collective's share of the step).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c1x256|c1|c0|c2|c4]
+  python bench.py --vocab-shard ...      # configuration 4 split by vocabulary as the headline
   python bench.py --impl reference ...   # the reference CPU sampler (oracle port)
 """
 from __future__ import annotations
@@ -144,25 +151,51 @@ def workload(name: str, rank: int, seed: int):
     return W.config(name, seed=seed + 7919 * rank)
 
 
-def cpu_baseline(batch, budget_s: float = 12.0):
-    """The oracle (a C++ port of the reference sampler) on the host cores, on a
-    bounded sample of the workload: batches of the workload's first rows, one
-    row per thread at a time, repeated until about budget_s of wall time."""
+def cpu_baseline(batch, budget_s: float = 12.0, gpu_tokens=None, parity_rows: int = 32):
+    """The CPU baseline leg: the oracle (a C++ port of the reference sampler)
+    on the host cores, on a bounded sample of the workload: batches of the
+    workload's first rows, one row per thread at a time, repeated until about
+    budget_s of wall time. As the checker, the same leg compares the GPU's
+    tokens for the workload's first `parity_rows` rows with the oracle's
+    (a mismatch counts as a boundary tie only when the oracle's own CDF or
+    top_p margin is below 1e-5 relative)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     threads = len(os.sched_getaffinity(0))
     n = min(batch.rows, 4 * threads)
     idx = np.arange(n)
     done, t0 = 0, time.perf_counter()
+    want = None
     while True:
-        O.sample_batch(batch.logits[idx], batch.params[idx], batch.hist[: batch.hist_off[n]],
-                       batch.hist_off[: n + 1], batch.uniforms[idx], threads=threads)
+        want = O.sample_batch(batch.logits[idx], batch.params[idx], batch.hist[: batch.hist_off[n]],
+                              batch.hist_off[: n + 1], batch.uniforms[idx], threads=threads)
         done += n
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+    base = {"value": done / dt, "unit": "rows/s", "cores": threads, "kind": "port",
             "sample": f"{done} rows of the {batch.name} workload ({n} per batch call) in {dt:.1f}s"}
+    parity = None
+    if gpu_tokens is not None:
+        parity = oracle_parity(O, batch, gpu_tokens, want, min(parity_rows, n))
+    return base, parity
+
+
+def oracle_parity(O, batch, gpu_tokens, want, rows):
+    lf = batch.logits_f32()
+    ident = ties = bad = 0
+    for r in range(rows):
+        if gpu_tokens[r] == want[r]:
+            ident += 1
+            continue
+        hist = batch.hist[batch.hist_off[r]: batch.hist_off[r + 1]].astype(np.int64).astype(np.uint32)
+        res = O.sample(lf[r], hist, batch.params[r], u=float(batch.uniforms[r]))
+        if res.debug.cdf_margin < 1e-5 or res.debug.topp_margin < 1e-5:
+            ties += 1
+        else:
+            bad += 1
+    return {"rows": rows, "identical": ident, "boundary_ties": ties, "mismatches": bad,
+            "checker": "oracle (C++ restatement of src/sampling/mod.rs)"}
 
 
 def run_reference(args):
@@ -170,12 +203,12 @@ def run_reference(args):
     if rank != 0:
         return
     batch = workload(args.workload, 0, args.seed)
-    base = cpu_baseline(batch, budget_s=max(5.0, 0.5 * (args.steps + args.warmup)))
+    base, _ = cpu_baseline(batch, budget_s=max(5.0, 0.5 * (args.steps + args.warmup)))
     line = {
         "impl": "reference", "metric": "sampled rows/sec at V=151,936", "value": base["value"],
         "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * batch.rows / base["value"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": batch.dtype if batch.dtype != "f32" else "f32",
+        "scaling": "weak", "vs_baseline": None, "dtype": batch.dtype,
         "data": "synthetic", "config": config_dict(batch, args, None),
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -195,78 +228,186 @@ def config_dict(batch, args, nbuf):
     return d
 
 
+def timed_passes(step, steps, stream, world, min_s=0.4, max_passes=400):
+    """Times `steps` steps per pass with CUDA events on the launching stream,
+    repeating passes until about min_s of device time has run, after one
+    barrier + synchronize; the passes' times are maxed over ranks pass by
+    pass. Returns (median pass ms, pass stats)."""
+    import torch
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for i in range(steps):
+        step(i)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    first = ev[0].elapsed_time(ev[1])
+    passes = int(max(1, min(max_passes, math.ceil(min_s * 1000.0 / max(first, 1e-3)))))
+    passes = int(max_over_ranks(float(passes), world))   # every rank runs the same passes
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(passes + 1)]
+    barrier(world)
+    torch.cuda.synchronize()
+    evs[0].record(stream)
+    for p in range(passes):
+        for i in range(steps):
+            step(p * steps + i)
+        evs[p + 1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = [evs[p].elapsed_time(evs[p + 1]) for p in range(passes)]
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor(ms, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.cpu().tolist()
+    med = statistics.median(ms)
+    return med, {"passes": passes, "steps_per_pass": steps, "pass_ms_median": round(med, 5),
+                 "pass_ms_min": round(min(ms), 5), "pass_ms_max": round(max(ms), 5),
+                 "timed_device_ms_total": round(sum(ms), 3)}
+
+
+def device_logits(batch, dev, nbuf=1):
+    """nbuf device copies of the batch's logits with distinct contents (ids
+    rolled), enough of them to exceed 2x L2 when nbuf is chosen so."""
+    import torch
+    if batch.dtype == "f32":
+        base = torch.from_numpy(batch.logits)
+    else:
+        base = torch.from_numpy(batch.logits.view(np.int16)).view(torch.bfloat16)
+    return [torch.roll(base, shifts=i * 977, dims=1).to(dev).contiguous() if i else base.to(dev)
+            for i in range(nbuf)]
+
+
+class SampleStep:
+    """One tqfs_sample call per step over rotating device buffers."""
+
+    def __init__(self, batch, dev, h, stream, nbuf=1):
+        import torch
+        import turboqwenfare_b200._native as N
+        from turboqwenfare_b200.sampler import params_tensor
+        self.batch, self.h, self.L = batch, h, N.lib()
+        self.bufs = device_logits(batch, dev, nbuf)
+        self.hist = torch.from_numpy(batch.hist if batch.hist.size else np.zeros(1, np.int32)).to(dev)
+        self.off = torch.from_numpy(batch.hist_off).to(dev)
+        self.params = params_tensor(batch.params, batch.rows, dev)
+        self.uni = torch.from_numpy(batch.uniforms).to(dev)
+        self.tokens = torch.empty(batch.rows, dtype=torch.int32, device=dev)
+        self.sp = stream.cuda_stream
+        self.dt = N.DTYPE_F32 if batch.dtype == "f32" else N.DTYPE_BF16
+
+    def __call__(self, i):
+        b = self.bufs[i % len(self.bufs)]
+        bt = self.batch
+        st = self.L.tqfs_sample(self.h.ptr, b.data_ptr(), self.dt, bt.rows, bt.vocab, bt.vocab,
+                                self.hist.data_ptr(), self.off.data_ptr(), self.params.data_ptr(),
+                                self.uni.data_ptr(), None, self.tokens.data_ptr(), None, None, None, self.sp)
+        if st != 0:
+            self.h.check(st)
+
+
+def kernel_times(h, step, steps):
+    """Per-launch device time of each library kernel (the library's own CUDA
+    events around every launch; kernels run back to back in this mode)."""
+    import turboqwenfare_b200._native as N
+    L = N.lib()
+    L.tqfs_set_timing(h.ptr, 1)
+    for i in range(steps):
+        step(i)
+    kms = (ctypes.c_float * 5)()
+    launches = (ctypes.c_int64 * 5)()
+    L.tqfs_get_timing(h.ptr, 5, kms, launches)
+    L.tqfs_set_timing(h.ptr, 0)
+    names = ["stream_kernel", "general_kernel", "window_kernel", "mtp_kernels", "finalize_kernel"]
+    return {names[i]: (kms[i] / launches[i] if launches[i] else 0.0) for i in range(5)}
+
+
+def run_other_workloads(args, rank, world, local, h, stream, peak):
+    """Configurations 2 and 3 on this rank (weak scaling: each rank its own
+    rows), timed like the headline; their lines' figures go into the
+    headline's JSON under `other_workloads`."""
+    import torch
+    import turboqwenfare_b200._native as N
+    from turboqwenfare_b200 import workloads as W
+    from turboqwenfare_b200.sampler import params_tensor
+    dev = torch.device("cuda", local)
+    out = {}
+    c2 = W.config("c2", seed=args.seed + 7919 * rank)
+    st2 = SampleStep(c2, dev, h, stream, nbuf=max(1, math.ceil(2 * L2_BYTES / c2.logits.nbytes) + 1))
+    for i in range(3):
+        st2(i)
+    ms, stats = timed_passes(st2, 20, stream, world, min_s=0.2)
+    alg = c2.algorithmic_bytes()
+    kt = kernel_times(h, st2, 10)
+    out["c2"] = {"rows_per_gpu": c2.rows, "dtype": "bf16", "ms_per_step": round(ms / 20, 5),
+                 "value": round(c2.rows * world * 20 / (ms / 1000.0), 1), "unit": "rows/s",
+                 "whole_step_hbm_frac": round(alg / (ms / 20 / 1000.0) / 1e9 / peak, 4),
+                 "algorithmic_bytes": alg, "kernel_us": {k: round(v * 1000, 2) for k, v in kt.items() if v},
+                 "general_rows": int(((c2.params["top_k"] == 0) & (c2.params["temperature"] > 0)).sum()),
+                 "timing": stats}
+    del st2
+    m = W.mtp_config(seed=args.seed + 7919 * rank)
+    S, Ld, V = m.seqs, m.draft_len, m.target.shape[-1]
+    tgt = torch.from_numpy(m.target).to(dev)
+    dft = torch.from_numpy(m.draft).to(dev)
+    drafts = torch.from_numpy(m.drafts).to(dev)
+    params = params_tensor(m.params, S, dev)
+    uni = torch.from_numpy(m.uniforms).to(dev)
+    acc = torch.empty(S, dtype=torch.int32, device=dev)
+    tok = torch.empty(S, dtype=torch.int32, device=dev)
+    L = N.lib()
+
+    def mtp_step(i):
+        r = L.tqfs_mtp_verify(h.ptr, tgt.data_ptr(), dft.data_ptr(), N.DTYPE_F32, S, Ld, V, V, drafts.data_ptr(),
+                              params.data_ptr(), uni.data_ptr(), acc.data_ptr(), tok.data_ptr(), None, None,
+                              stream.cuda_stream)
+        if r != 0:
+            h.check(r)
+
+    for i in range(3):
+        mtp_step(i)
+    ms, stats = timed_passes(mtp_step, 10, stream, world, min_s=0.2)
+    alg = m.algorithmic_bytes()
+    out["c3"] = {"seqs_per_gpu": S, "draft_len": Ld, "ms_per_call": round(ms / 10, 5),
+                 "value": round(S * (Ld + 1) * world * 10 / (ms / 1000.0), 1), "unit": "verified target rows/s",
+                 "whole_call_hbm_frac": round(alg / (ms / 10 / 1000.0) / 1e9 / peak, 4),
+                 "algorithmic_bytes": alg, "l2": "inputs resident (136 MB, about L2 size), no flush",
+                 "timing": stats}
+    return out
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import turboqwenfare_b200._native as N
-    from turboqwenfare_b200.sampler import params_tensor
 
     batch = workload(args.workload, rank, args.seed)
-    esz = 4 if batch.dtype == "f32" else 2
     nbuf = max(1, math.ceil(2 * L2_BYTES / batch.logits.nbytes) + 1)
-    if batch.dtype == "f32":
-        base = torch.from_numpy(batch.logits)
-    else:
-        base = torch.from_numpy(batch.logits.view(np.int16)).view(torch.bfloat16)
-    bufs = []
-    for i in range(nbuf):  # distinct contents per buffer (rolled ids)
-        bufs.append(torch.roll(base, shifts=i * 977, dims=1).to(dev).contiguous() if i else base.to(dev))
-    hist = torch.from_numpy(batch.hist).to(dev)
-    off = torch.from_numpy(batch.hist_off).to(dev)
-    params = params_tensor(batch.params, batch.rows, dev)
-    uni = torch.from_numpy(batch.uniforms).to(dev)
-    tokens = torch.empty(batch.rows, dtype=torch.int32, device=dev)
     h = N.Handle(local)
     L = N.lib()
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
-    dt = N.DTYPE_F32 if batch.dtype == "f32" else N.DTYPE_BF16
-
-    def step(i):
-        b = bufs[i % nbuf]
-        st = L.tqfs_sample(h.ptr, b.data_ptr(), dt, batch.rows, batch.vocab, batch.vocab, hist.data_ptr(),
-                           off.data_ptr(), params.data_ptr(), uni.data_ptr(), None, tokens.data_ptr(), None, None,
-                           None, sp)
-        if st != 0:
-            h.check(st)
-
+    step = SampleStep(batch, dev, h, stream, nbuf)
+    dt = step.dt
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize()
 
-    # ---- value: K steps, events on the launching stream, max over ranks ----
+    # ---- value: passes of exactly K steps, events on the launching stream,
+    # each pass maxed over ranks; the median pass is reported --------------
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = e0.elapsed_time(e1)
+    pass_ms, timing = timed_passes(step, args.steps, stream, world)
     clk = clocks.stop()
-    ms = max_over_ranks(ms, world)
-    ms_per_step = ms / args.steps
-    value = batch.rows * world * args.steps / (ms / 1000.0)
+    ms_per_step = pass_ms / args.steps
+    value = batch.rows * world * args.steps / (pass_ms / 1000.0)
 
     # ---- dominant kernel: per-launch duration from the library's events ----
-    L.tqfs_set_timing(h.ptr, 1)
-    for i in range(args.steps):
-        step(i)
-    kms = (ctypes.c_float * 5)()
-    launches = (ctypes.c_int64 * 5)()
-    L.tqfs_get_timing(h.ptr, 5, kms, launches)
-    L.tqfs_set_timing(h.ptr, 0)
-    kernel_ms = kms[0] / max(1, launches[0])
-    window_ms = kms[2] / max(1, launches[2])
-    general_ms = kms[1] / max(1, launches[1])
-    finalize_ms = kms[4] / max(1, launches[4])
+    kt = kernel_times(h, step, args.steps)
+    kernel_ms = kt["stream_kernel"]
     alg_bytes = batch.algorithmic_bytes()
     peak, peak_kind = measured_hbm_peak()
     achieved = alg_bytes / (kernel_ms / 1000.0) / 1e9
@@ -274,9 +415,8 @@ def run_ours(args):
             "frac": round(achieved / peak, 4), "peak_source": peak_kind,
             "kernel": "stream_kernel", "kernel_us": round(kernel_ms * 1000, 2),
             "algorithmic_bytes_per_launch": alg_bytes,
-            "other_kernels_us": {"window_kernel": round(window_ms * 1000, 2),
-                                 "finalize_kernel": round(finalize_ms * 1000, 2),
-                                 "general_kernel": round(general_ms * 1000, 2)},
+            "other_kernels_us": {k: round(v * 1000, 2) for k, v in kt.items()
+                                 if k != "stream_kernel" and k != "mtp_kernels"},
             "traffic": None}
     tpath = os.path.join(ROOT, "profiles", "stream_kernel_traffic.json")
     if os.path.exists(tpath):
@@ -286,6 +426,11 @@ def run_ours(args):
                 roof["traffic"] = tr["bytes_per_launch"]
         except Exception:
             pass
+
+    # the tokens of the first buffer (the batch's own logits), for the checker
+    step(0)
+    torch.cuda.synchronize()
+    tokens0 = step.tokens.cpu().numpy().copy()
 
     # ---- e2e through the host-buffer C ABI (H2D + sample + D2H per step) ----
     pinned = torch.empty(batch.logits.shape, dtype=torch.float32 if batch.dtype == "f32" else torch.int16,
@@ -312,27 +457,36 @@ def run_ours(args):
     for _ in range(args.e2e_steps):
         e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    h2d = int(batch.logits.nbytes + batch.hist.nbytes + batch.hist_off.nbytes + batch.params.nbytes
+              + batch.uniforms.nbytes)
     e2e = {"value": batch.rows * world * args.e2e_steps / e2e_s, "unit": "rows/s",
-           "h2d_bytes_per_step": int(batch.logits.nbytes + batch.hist.nbytes + batch.hist_off.nbytes
-                                     + batch.params.nbytes + batch.uniforms.nbytes),
-           "d2h_bytes_per_step": int(tok_h.numel() * 4), "api": "tqfs_sample_host"}
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(tok_h.numel() * 4), "api": "tqfs_sample_host",
+           "h2d_gbs_per_gpu": round(h2d * args.e2e_steps / e2e_s / 1e9, 1)}
+    del pinned
 
-    base = None
+    others = run_other_workloads(args, rank, world, local, h, stream, peak)
+    vshard = run_vocab_split(args, rank, world, local) if world > 1 else None
+
+    base = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(batch)
+        base, parity = cpu_baseline(batch, gpu_tokens=tokens0)
 
-    # launches of our kernels inside the timed region: the window pre-pass
+    # launches of our kernels inside the timed passes: the window pre-pass
     # (rows with a history), the stream, finalize and general kernels
     per_step_launches = 3 + (1 if batch.hist_off is not None else 0)
     line = {
         "metric": "sampled rows/sec at V=151,936", "value": round(value, 1), "unit": "rows/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if batch.dtype == "f32" else "bf16", "data": "synthetic",
+        "dtype": batch.dtype, "data": "synthetic",
         "config": config_dict(batch, args, nbuf), "roofline": roof, "cpu_baseline": base, "e2e": e2e,
-        "gpu_launches": args.steps * per_step_launches, "clocks": clk,
+        "gpu_launches": args.steps * timing["passes"] * per_step_launches, "clocks": clk, "timing": timing,
         "hbm_gbs_whole_step": round(alg_bytes / (ms_per_step / 1000.0) / 1e9, 1),
+        "whole_step_hbm_frac": round(alg_bytes / (ms_per_step / 1000.0) / 1e9 / peak, 4),
+        "parity": parity, "other_workloads": others,
     }
+    if vshard is not None:
+        line["vocab_shard"] = vshard
     if rank == 0:
         print(json.dumps(line), flush=True)
     h.close()
@@ -341,18 +495,23 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_vocab_sharded(args):
-    """Configuration 4: every rank holds all rows' ids [offset, offset + V/N);
-    one step = export, NCCL all-gather, merge and draw on every rank. Total
-    work is fixed as N grows (strong scaling)."""
+def run_vocab_split(args, rank, world, local, steps=20):
+    """Configuration 4 split by vocabulary over the job's ranks: every rank
+    holds ids [offset, offset + V/N) of the same 1,024 bf16 rows; one step =
+    per-shard export, one NCCL all-gather of the records, merge and draw on
+    every rank (tqfs_sample_vocab_sharded). Strong scaling. Also timed in
+    parts (export, all-gather of the records through torch.distributed's
+    NCCL, merge) for the collective's share, and checked: rank 0's tokens
+    against the unsharded call on its own GPU."""
     import torch
-    rank, world, local = dist_setup(args.gpus)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    import torch.distributed as dist
     from turboqwenfare_b200 import workloads as W
-    from turboqwenfare_b200.sampler import params_tensor
-    from turboqwenfare_b200.sharding import NcclComm, sample_vocab_sharded, vocab_shards
-    batch = W.config("c4", seed=args.seed)  # the same rows on every rank
+    from turboqwenfare_b200.sampler import params_tensor, sample_batch
+    from turboqwenfare_b200.sharding import (NcclComm, record_words, sample_vocab_sharded, shard_export,
+                                             shard_merge, vocab_shards)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    batch = W.config("c4", seed=args.seed)          # the same rows on every rank
     off0, n = vocab_shards(batch.vocab, world)[rank]
     full = torch.from_numpy(batch.logits.view(np.int16)).view(torch.bfloat16)
     nbuf = max(1, math.ceil(2 * L2_BYTES / (batch.rows * n * 2)) + 1)
@@ -361,145 +520,81 @@ def run_vocab_sharded(args):
     hoff = torch.from_numpy(batch.hist_off).to(dev)
     params = params_tensor(batch.params, batch.rows, dev)
     uni = torch.from_numpy(batch.uniforms).to(dev)
-    if world > 1:
-        comm = NcclComm(rank, world, local)
-    else:
-        import torch.distributed as dist
-        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % _free_port(), rank=0, world_size=1)
-        comm = NcclComm(0, 1, local)
+    comm = NcclComm(rank, world, local)
+    out = {}
 
     def step(i):
-        sample_vocab_sharded(comm, bufs[i % nbuf], params, off0, batch.vocab, uniforms=uni, history=hist,
-                             history_offsets=hoff)
+        out["r"] = sample_vocab_sharded(comm, bufs[i % nbuf], params, off0, batch.vocab, uniforms=uni,
+                                        history=hist, history_offsets=hoff)
 
-    for i in range(max(args.warmup, 3)):
+    for i in range(3):
         step(i)
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(dev)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
+    ms, stats = timed_passes(step, steps, stream, world, min_s=0.2)
+    # parts: export, all-gather, merge, each with its own events
+    words = record_words()
+    recs = torch.empty((batch.rows, words), dtype=torch.int64, device=dev)
+    gathered = torch.empty((world, batch.rows, words), dtype=torch.int64, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    part = [0.0, 0.0, 0.0]
     barrier(world)
+    for i in range(steps):
+        ev[0].record(stream)
+        shard_export(bufs[i % nbuf], params, off0, batch.vocab, history=hist, history_offsets=hoff, records=recs)
+        ev[1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, recs)
+        else:
+            gathered[0].copy_(recs)
+        ev[2].record(stream)
+        shard_merge(gathered, params, batch.vocab, uniforms=uni, history_offsets=hoff)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        for j in range(3):
+            part[j] += ev[j].elapsed_time(ev[j + 1])
+    part = [max_over_ranks(x / steps, world) for x in part]
+    # check: rank 0's sharded tokens (the batch's own logits) == the whole-row call
+    step(0)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    clk = clocks.stop()
-    ms_per_step = ms / args.steps
-    alg = batch.rows * batch.vocab * 2 + 4 * int(batch.hist_off[-1]) * world
-    line = {
-        "metric": "sampled rows/sec at V=151,936", "value": round(batch.rows * args.steps / (ms / 1000.0), 1),
-        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "c4", "rows": batch.rows, "vocab": batch.vocab, "vocab_per_gpu": n,
-                   "parallelism": f"vocabulary split over {world} GPU(s), NCCL all-gather of per-shard top-50",
-                   "l2": f"{nbuf} rotating input buffers", "seed": args.seed},
-        "hbm_gbs_whole_step": round(alg / world / (ms_per_step / 1000.0) / 1e9, 1),
-        "gpu_launches": args.steps * 4, "clocks": clk,  # window, stream, finalize (export), merge
-    }
+    tok, st = (t.cpu().numpy() for t in out["r"])
+    agree = None
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        whole = sample_batch(full.to(dev), params, hist, hoff, uniforms=uni, vocab=batch.vocab)
+        torch.cuda.synchronize()
+        agree = bool((tok == whole.tokens.cpu().numpy()).all() and (st == 0).all())
     comm.close()
-    import torch.distributed as dist
-    if dist.is_initialized():
-        dist.destroy_process_group()
+    ms_step = ms / steps
+    return {"workload": "c4", "rows": batch.rows, "vocab_per_gpu": n, "n_gpus": world,
+            "ms_per_step": round(ms_step, 5), "value": round(batch.rows * steps / (ms / 1000.0), 1),
+            "unit": "rows/s", "scaling": "strong",
+            "parts_ms": {"export": round(part[0], 5), "all_gather": round(part[1], 5), "merge": round(part[2], 5)},
+            "all_gather_share": round(part[1] / max(1e-9, sum(part)), 4),
+            "all_gather_bytes_per_rank": int(batch.rows * words * 8),
+            "tokens_equal_unsharded": agree, "timing": stats}
 
 
-def run_mtp(args):
-    """Configuration 3: MTP verify of 32 sequences x (3 drafts + bonus) per
-    call (tqfs_mtp_verify). The metric counts the target rows a call verifies
-    (seqs x (L + 1)); rows shard across ranks with no collective."""
-    import ctypes
+def run_vocab_sharded(args):
+    """`--vocab-shard`: configuration 4 split by vocabulary as the headline
+    line (strong scaling)."""
     import torch
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    import turboqwenfare_b200._native as N
-    from turboqwenfare_b200 import workloads as W
-    from turboqwenfare_b200.sampler import params_tensor
-    m = W.mtp_config(seed=args.seed + 7919 * rank)
-    S, L, V = m.seqs, m.draft_len, m.target.shape[-1]
-    rows = S * (L + 1)
-    tgt = torch.from_numpy(m.target).to(dev)
-    dft = torch.from_numpy(m.draft).to(dev)
-    drafts = torch.from_numpy(m.drafts).to(dev)
-    params = params_tensor(m.params, S, dev)
-    uni = torch.from_numpy(m.uniforms).to(dev)
-    acc = torch.empty(S, dtype=torch.int32, device=dev)
-    tok = torch.empty(S, dtype=torch.int32, device=dev)
-    mask = torch.empty((S, L), dtype=torch.uint8, device=dev)
-    st = torch.empty(S, dtype=torch.int32, device=dev)
-    h = N.Handle(local)
-    Lb = N.lib()
-    sp = torch.cuda.current_stream(dev).cuda_stream
-
-    def call(t_ptr, d_ptr):
-        r = Lb.tqfs_mtp_verify(h.ptr, t_ptr, d_ptr, N.DTYPE_F32, S, L, V, V, drafts.data_ptr(),
-                               params.data_ptr(), uni.data_ptr(), acc.data_ptr(), tok.data_ptr(),
-                               mask.data_ptr(), st.data_ptr(), sp)
-        if r != 0:
-            h.check(r)
-
-    for _ in range(max(args.warmup, 3)):
-        call(tgt.data_ptr(), dft.data_ptr())
-    torch.cuda.synchronize()
+    if world == 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % _free_port(), rank=0, world_size=1)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        call(tgt.data_ptr(), dft.data_ptr())
-    e1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    r = run_vocab_split(args, rank, world, local, steps=args.steps)
     clk = clocks.stop()
-    ms_per_step = ms / args.steps
-    # e2e: the rows copied from pinned host memory each call, the results back
-    th = torch.from_numpy(m.target).pin_memory()
-    dh = torch.from_numpy(m.draft).pin_memory()
-    out_h = torch.empty(S, dtype=torch.int32, pin_memory=True)
-    torch.cuda.synchronize()
-    e2 = max(3, args.e2e_steps)
-    t0 = time.perf_counter()
-    for _ in range(e2):
-        tgt.copy_(th, non_blocking=True)
-        dft.copy_(dh, non_blocking=True)
-        call(tgt.data_ptr(), dft.data_ptr())
-        out_h.copy_(tok, non_blocking=True)
-        torch.cuda.synchronize()
-    e2e_s = (time.perf_counter() - t0) / e2
-    base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-        done, t1 = 0, time.perf_counter()
-        while time.perf_counter() - t1 < 10.0:
-            O.mtp_verify(m.target, m.draft, m.drafts.astype(np.uint32), m.params, m.uniforms)
-            done += rows
-        dt = time.perf_counter() - t1
-        base = {"value": done / dt, "unit": "rows/s", "cores": 1, "kind": "port",
-                "sample": f"{done // rows} oracle verify calls of configuration 3 in {dt:.1f}s"}
     line = {
-        "metric": "verified target rows/sec at V=151,936", "value": round(rows * world * args.steps / (ms / 1000.0), 1),
-        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c3", "seqs_per_gpu": S, "draft_len": L, "vocab": V, "temperature": 0.8,
-                   "top_p": 0.9, "l2": "inputs resident (78 MB), no flush"},
-        "cpu_baseline": base,
-        "e2e": {"value": round(rows * world / e2e_s, 1), "unit": "rows/s",
-                "h2d_bytes_per_step": int(m.target.nbytes + m.draft.nbytes), "d2h_bytes_per_step": 4 * S},
-        "gpu_launches": args.steps * 2, "clocks": clk,  # the row kernel and the decide kernel
+        "metric": "sampled rows/sec at V=151,936", "value": r["value"], "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "c4", "rows": r["rows"], "vocab_per_gpu": r["vocab_per_gpu"],
+                   "parallelism": f"vocabulary split over {world} GPU(s), NCCL all-gather of per-shard top-50",
+                   "seed": args.seed},
+        "gpu_launches": args.steps * r["timing"]["passes"] * 4, "clocks": clk, "vocab_shard": r,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -521,8 +616,6 @@ def main():
         run_reference(args)
     elif args.vocab_shard:
         run_vocab_sharded(args)
-    elif args.workload == "c3":
-        run_mtp(args)
     else:
         run_ours(args)
 

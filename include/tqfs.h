@@ -2,7 +2,7 @@
  * tqfs.h — C ABI of libtqfsample, the sm_100a token-sampling library.
  *
  * This is the boundary a Rust `src/backend/cuda` module binds with
- * `extern "C"` (see INTEGRATION.md for the binding). Every entry point takes
+ * `extern "C"`. Every entry point takes
  * plain pointers and sizes; no C++ or PyTorch types cross it. Reference
  * interfaces are cited by path:line inside the TurboQwenFare crate.
  *
@@ -108,6 +108,20 @@ const char* tqfs_last_error(const tqfs_handle* handle);
  * kernel. Test and benchmark instrumentation only. */
 int tqfs_set_timing(tqfs_handle* handle, int enabled);
 int tqfs_get_timing(tqfs_handle* handle, int n, float* kernel_ms, int64_t* launches);
+/* How the stream kernel splits a batch on the current device: each logits
+ * row is cut into 2,048-id chunks and into *units_per_row runs of up to
+ * *chunks_per_unit chunks, one warp per run. Diagnostics only. */
+int tqfs_stream_plan(int rows, int vocab, int dtype, int* units_per_row, int* chunks_per_unit);
+/* Test instrumentation, for the next stream-path call on this handle only
+ * (tqfs_sample, tqfs_top_logit_candidates, tqfs_shard_export): the bulk copies
+ * of logits row `row` are armed on their barriers but never issued, and every
+ * copy wait gives up after wait_ns. The waits for that row run out; the row,
+ * and any row a warp that gave up would have handled afterwards, report
+ * TQFS_ROW_ERR_TIMEOUT with token -1, and the call completes. Rows whose ld
+ * or base is not 16-byte aligned are copied without bulk copies and never
+ * stall. No counterpart in the reference (its waits are host fences,
+ * src/backend/metal/timing.rs:68-79). */
+int tqfs_debug_stall_row(tqfs_handle* handle, int row, uint64_t wait_ns);
 
 /* ---- host RNG helpers (no device work) ---------------------------------- */
 /* `Xoshiro256PlusPlus::from_seed` (src/sampling/mod.rs:283-295). */
@@ -279,9 +293,10 @@ int tqfs_sample_vocab_sharded(tqfs_handle* handle, void* comm, int nranks, const
  *     TQFS_ROW_ERR_UNSUPPORTED and token -1.
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
- *   - All calls share the array and leave its contents behind; no part of
- *     it needs clearing, as each call writes what it later reads. Calls that
- *     overlap on the GPU race on it and must not be issued.
+ *   - All calls share the array and leave its contents behind. Only one
+ *     word per row must start at zero; each call zeroes it in stream order
+ *     (its first kernel and its last). Calls that overlap on the GPU race on
+ *     the array and must not be issued.
  */
 int tqfs_sample_static(const void* logits_dev, int dtype, int rows, int vocab, int64_t ld,
                        const int32_t* hist_dev, const int64_t* hist_off_dev,

@@ -36,7 +36,7 @@ PARAM_HAS_MIN_P = 1
 # Every symbol include/tqfs.h declares; tests check the library exports them.
 EXPORTS = [
     "tqfs_version", "tqfs_status_string", "tqfs_create", "tqfs_destroy", "tqfs_last_error",
-    "tqfs_set_timing", "tqfs_get_timing", "tqfs_xoshiro_from_seed", "tqfs_xoshiro_next_u64",
+    "tqfs_set_timing", "tqfs_get_timing", "tqfs_stream_plan", "tqfs_debug_stall_row", "tqfs_xoshiro_from_seed", "tqfs_xoshiro_next_u64",
     "tqfs_xoshiro_next_f32", "tqfs_sample", "tqfs_sample_host", "tqfs_top_logit_candidates",
     "tqfs_apply_penalties", "tqfs_mtp_verify", "tqfs_shard_record_words", "tqfs_shard_export",
     "tqfs_shard_merge", "tqfs_nccl_unique_id", "tqfs_nccl_comm_init", "tqfs_nccl_comm_destroy",
@@ -95,6 +95,8 @@ def lib() -> ctypes.CDLL:
     L.tqfs_last_error.restype = ctypes.c_char_p
     L.tqfs_set_timing.argtypes = [vp, i32]
     L.tqfs_get_timing.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int64)]
+    L.tqfs_debug_stall_row.argtypes = [vp, i32, u64]
+    L.tqfs_stream_plan.argtypes = [i32, i32, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)]
     L.tqfs_xoshiro_from_seed.argtypes = [u64, u64p]
     L.tqfs_xoshiro_from_seed.restype = None
     L.tqfs_xoshiro_next_u64.argtypes = [u64p]
@@ -161,6 +163,14 @@ class Handle:
 
 
 _handles: dict[int, Handle] = {}
+
+
+def stream_plan(rows: int, vocab: int, dtype: int = DTYPE_F32) -> tuple[int, int]:
+    """(units per row, chunks per unit) the stream kernel uses for a batch on
+    the current device."""
+    u, c = ctypes.c_int(), ctypes.c_int()
+    check(lib().tqfs_stream_plan(rows, vocab, dtype, ctypes.byref(u), ctypes.byref(c)))
+    return u.value, c.value
 
 
 def default_handle(device: int = 0) -> Handle:

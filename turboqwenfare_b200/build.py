@@ -44,18 +44,34 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles every source to an object in parallel, then links the shared
+    library (no device linking: no device code crosses translation units)."""
     if not force and not needs_build():
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
-    srcs = [os.path.join(CSRC, s) for s in SOURCES]
+    objs, procs = [], []
+    for s in SOURCES:
+        obj = os.path.join(LIB_DIR, s.replace(".cu", ".o"))
+        objs.append(obj)
+        cmd = [nvcc()] + flags(verbose) + ["-c", "-o", obj, os.path.join(CSRC, s)]
+        procs.append((s, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    failed = []
+    for s, p in procs:
+        out, err = p.communicate()
+        if p.returncode != 0:
+            failed.append(s)
+            sys.stderr.write(out + err)
+        elif verbose:
+            sys.stderr.write(err)
+    if failed:
+        raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
     tmp = LIB + ".tmp"
-    cmd = [nvcc()] + flags(verbose) + ["-shared", "-o", tmp] + srcs
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    res = subprocess.run([nvcc()] + ARCH + ["-shared", "-o", tmp] + objs, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libtqfsample.so")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("nvcc failed linking libtqfsample.so")
+    for obj in objs:
+        os.remove(obj)
     os.replace(tmp, LIB)
     return LIB
 

@@ -55,12 +55,13 @@ struct tqfs_handle {
     std::string error;
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
-    DeviceBuffer err_word;     // a call's number when one of its copy waits gave up
-    DeviceBuffer row_th;       // per-row bounds shared by a row's units, tagged by call
+    DeviceBuffer row_th;       // per-row word of a call (bound, timeout); zero between calls
     DeviceBuffer mtp;          // MTP verify workspaces
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
-    uint32_t epoch = 0;        // number of the last call
+    bool row_th_dirty = false; // a call launched the stream kernel but not its finalize
+    int stall_row_p1 = 0;      // test hook for the next call (tqfs_debug_stall_row)
+    unsigned long long stall_wait_ns = 0;
     size_t general_layout[3] = {0, 0, 0};
     // staging for the host-buffer entry points
     DeviceBuffer h_logits, h_hist, h_off, h_params, h_unif, h_rng, h_tok;
@@ -155,28 +156,53 @@ int ensure_current(tqfs_handle* h) {
 }
 
 // Scratch of the stream path (candidate lists, chunk bounds, greedy lists,
-// window buckets), grown on demand and never cleared: every field a kernel
-// reads is written earlier in the same call.
-int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::SampleArgs& a) {
+// window buckets), grown on demand; every field a kernel reads is written
+// earlier in the same call. The per-row words (row_th) must be zero when a
+// call starts: new memory is zeroed on the call's stream, and every call's
+// finalize kernel clears the words it read.
+int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::SampleArgs& a,
+                   cudaStream_t s) {
     const size_t bytes = tqfs::stream_scratch(rows, plan, nullptr, nullptr);
     cudaError_t e = h->scratch.reserve(bytes);
     if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     tqfs::stream_scratch(rows, plan, h->scratch.ptr, &a);
-    if (h->err_word.ptr == nullptr) {  // zero once; calls are told apart by epoch
-        e = h->err_word.reserve(16);
-        if (e == cudaSuccess) e = cudaMemset(h->err_word.ptr, 0, 16);
+    const size_t words = static_cast<size_t>(rows) * 8;
+    if (h->row_th.bytes < words || h->row_th_dirty) {
+        e = h->row_th.reserve(words);
+        if (e == cudaSuccess) e = cudaMemsetAsync(h->row_th.ptr, 0, h->row_th.bytes, s);
         if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
+        h->row_th_dirty = false;
     }
-    if (++h->epoch == 0u) h->epoch = 1u;
-    if (h->row_th.bytes < static_cast<size_t>(rows) * 8) {  // new memory starts at zero
-        e = h->row_th.reserve(static_cast<size_t>(rows) * 8);
-        if (e == cudaSuccess) e = cudaMemset(h->row_th.ptr, 0, h->row_th.bytes);
-        if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
-    }
-    a.err_word = static_cast<uint32_t*>(h->err_word.ptr);
     a.row_th = static_cast<unsigned long long*>(h->row_th.ptr);
-    a.epoch = h->epoch;
+    a.wait_ns = h->stall_wait_ns;       // 0: the kernels' default budget
+    a.stall_row_p1 = h->stall_row_p1;   // the test hook lasts one call
+    h->stall_wait_ns = 0;
+    h->stall_row_p1 = 0;
     return TQFS_OK;
+}
+
+// Launches the window pre-pass, the stream kernel and its finalize kernel.
+// A finalize that fails to launch after the stream kernel did leaves per-row
+// words set; the next call then zeroes them first.
+cudaError_t launch_stream_path(tqfs_handle* h, const tqfs::SampleArgs& a, const tqfs::Plan& plan,
+                               cudaStream_t s, bool window) {
+    cudaError_t e;
+    {
+        TimingScope ts(h, s, 2);
+        e = tqfs::launch_window(a, plan, s);
+    }
+    if (e != cudaSuccess) return e;
+    {
+        TimingScope ts(h, s, 0);
+        e = tqfs::launch_stream(a, plan, s, window && !h->timing);
+    }
+    if (e != cudaSuccess) return e;
+    {
+        TimingScope ts(h, s, 4);
+        e = tqfs::launch_finalize(a, plan, s, !h->timing);
+    }
+    if (e != cudaSuccess) h->row_th_dirty = true;
+    return e;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -190,26 +216,11 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     }
     const tqfs::Plan plan = tqfs::plan_stream(a.rows, a.vocab, a.dtype);
     if (plan.chunks == 0) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
-    int st = ensure_scratch(h, a.rows, plan, a);
+    int st = ensure_scratch(h, a.rows, plan, a, s);
     if (st != TQFS_OK) return st;
     const size_t esz = a.dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
-    cudaError_t e;
-    {
-        const bool window = a.hist_off != nullptr && !a.top4_only;
-        {
-            TimingScope ts(h, s, 2);
-            e = tqfs::launch_window(a, plan, s);
-        }
-        if (e == cudaSuccess) {
-            TimingScope ts(h, s, 0);
-            e = tqfs::launch_stream(a, plan, s, window && !h->timing);
-        }
-        if (e == cudaSuccess) {
-            TimingScope ts(h, s, 4);
-            e = tqfs::launch_finalize(a, plan, s, !h->timing);
-        }
-    }
+    cudaError_t e = launch_stream_path(h, a, plan, s, a.hist_off != nullptr && !a.top4_only);
     if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
     if (a.top4_only) return TQFS_OK;
     // Rows the stream kernel does not own run the general kernel.
@@ -313,7 +324,6 @@ int tqfs_destroy(tqfs_handle* h) {
     for (cudaEvent_t e : h->free_events) cudaEventDestroy(e);
     h->scratch.release();
     h->general.release();
-    h->err_word.release();
     h->row_th.release();
     h->mtp.release();
     h->shard_send.release();
@@ -340,6 +350,24 @@ int tqfs_set_timing(tqfs_handle* h, int enabled) {
         h->kernel_ms[i] = 0.0;
         h->launches[i] = 0;
     }
+    return TQFS_OK;
+}
+
+int tqfs_stream_plan(int rows, int vocab, int dtype, int* units_per_row, int* chunks_per_unit) {
+    if (rows <= 0 || vocab <= 0 || !units_per_row || !chunks_per_unit ||
+        (dtype != TQFS_DTYPE_F32 && dtype != TQFS_DTYPE_BF16))
+        return TQFS_ERR_INVALID_ARG;
+    const tqfs::Plan plan = tqfs::plan_stream(rows, vocab, dtype);
+    if (plan.chunks == 0) return TQFS_ERR_UNSUPPORTED;
+    *units_per_row = plan.units;
+    *chunks_per_unit = plan.unit_len;
+    return TQFS_OK;
+}
+
+int tqfs_debug_stall_row(tqfs_handle* h, int row, uint64_t wait_ns) {
+    if (!h || row < 0 || wait_ns == 0) return TQFS_ERR_INVALID_ARG;
+    h->stall_row_p1 = row + 1;
+    h->stall_wait_ns = wait_ns;
     return TQFS_OK;
 }
 
@@ -603,22 +631,10 @@ int tqfs_shard_export(tqfs_handle* h, const void* logits_dev, int dtype, int row
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const tqfs::Plan plan = tqfs::plan_stream(a.rows, a.vocab, a.dtype);
     if (plan.chunks == 0) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", a.vocab);
-    if ((st = ensure_scratch(h, a.rows, plan, a)) != TQFS_OK) return st;
+    if ((st = ensure_scratch(h, a.rows, plan, a, s)) != TQFS_OK) return st;
     const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
-    cudaError_t e;
-    {
-        TimingScope ts(h, s, 2);
-        e = tqfs::launch_window(a, plan, s);
-    }
-    if (e == cudaSuccess) {
-        TimingScope ts(h, s, 0);
-        e = tqfs::launch_stream(a, plan, s, hist_off_dev != nullptr && !h->timing);
-    }
-    if (e == cudaSuccess) {
-        TimingScope ts(h, s, 4);
-        e = tqfs::launch_finalize(a, plan, s, !h->timing);
-    }
+    const cudaError_t e = launch_stream_path(h, a, plan, s, hist_off_dev != nullptr);
     return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "shard export launch");
 }
 

@@ -26,6 +26,8 @@ constexpr int kChunkCap = 256;       // candidate keys kept per (row, chunk)
 constexpr int kWinCap = 8192;        // penalty-window tokens the stream path buckets
 constexpr int kMaxChunks = 512;      // chunks per row (8 KiB of logits each)
 constexpr int kShardRec = 2 + kStreamMaxK;  // u64 per row in a vocabulary shard's record
+constexpr unsigned long long kRowFailed = 1ull << 63;      // row word: a copy wait gave up
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s per bounded copy wait
 
 // Which kernel owns a row.
 enum : int { kModeGreedy = 0, kModeStream = 1, kModeGeneral = 2 };

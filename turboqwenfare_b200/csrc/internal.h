@@ -37,9 +37,13 @@ struct SampleArgs {
     int chunk_len;             // ids per chunk
     int unit_len;              // chunks per unit (a warp's run of one row)
     int units;                 // units per row
-    uint32_t* err_word;        // set to `epoch` when a bounded wait gives up
-    unsigned long long* row_th;  // rows: (epoch << 32) | the largest unit bound published
-    uint32_t epoch;            // this call's number (never 0)
+    // rows: the largest k-th bound a unit of the row published (low 32 bits)
+    // and kRowFailed when a copy wait of the row gave up. Zero when a call
+    // starts: the finalize kernel clears each row's word after reading it.
+    unsigned long long* row_th;
+    unsigned long long wait_ns;  // budget of each bounded copy wait (0: kDefaultWaitNs)
+    int stall_row_p1;          // test hook: 1 + the row whose copies are armed but never
+                               // issued, so its waits run out (0: none)
     int vec_ok;                // rows start on 16-byte boundaries
     int vocab_route;           // vocabulary the routing compares top_k with
     int vocab_offset;          // global id of this shard's first id

@@ -14,11 +14,13 @@
 // stream path's per-row scratch: 34 to 48 KiB per row at vocab 151,936 (the
 // split of rows into work units depends on the batch), so up to about 1,300
 // rows of that width; a call that needs more returns TQFS_ERR_UNSUPPORTED.
-// Every call on a device uses the same array and leaves its contents behind;
-// nothing in it has to start at zero, because every field a kernel reads is
-// written earlier in the same call. Calls that overlap on the GPU (different
-// streams, or host threads without ordering) race on the array and must not
-// be issued.
+// Every call on a device uses the same array and leaves its contents behind.
+// The candidate lists and window buckets need no clearing: every field a
+// kernel reads is written earlier in the same call. The one word per row
+// that must start at zero (the row's shared k-th bound and its timeout mark)
+// is zeroed by the call's first kernel and again by its finalize kernel, both
+// in stream order. Calls that overlap on the GPU (different streams, or host
+// threads without ordering) race on the array and must not be issued.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,47 +34,42 @@ namespace {
 constexpr size_t kStaticBytes = static_cast<size_t>(48) << 20;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
-static __device__ uint32_t g_static_err;  // zero at load; see SampleArgs::epoch
 constexpr int kStaticRows = 4096;
-static __device__ unsigned long long g_static_row_th[kStaticRows];  // zero at load; tagged by epoch
+static __device__ unsigned long long g_static_row_th[kStaticRows];  // per-row words, see SampleArgs
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
-void* g_err_addr[kMaxDevices] = {};
 void* g_row_th_addr[kMaxDevices] = {};
-uint32_t g_epoch[kMaxDevices] = {};
 
-// Rows the stream kernel does not own (general rows) keep this status.
-__global__ void mark_unhandled_kernel(int rows, int32_t* out_token, int32_t* out_status) {
+// Rows the stream kernel does not own (general rows) keep this status; the
+// row words of the call's rows start at zero.
+__global__ void mark_unhandled_kernel(int rows, int32_t* out_token, int32_t* out_status,
+                                      unsigned long long* row_th) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     if (out_token) out_token[r] = -1;
     if (out_status) out_status[r] = TQFS_ROW_ERR_UNSUPPORTED;
+    row_th[r] = 0ull;
 }
 
-// Device address of g_static_scratch on the current device. In host code the
-// symbol names a host-side stand-in, not device memory, so the address is
-// looked up once per device (with that device current) and cached.
-// Also hands out the call's epoch (never 0).
-cudaError_t static_scratch(int device, void** out, uint32_t** err, uint32_t* epoch) {
+// Device addresses of the static arrays on the current device. In host code
+// a __device__ symbol names a host-side stand-in, not device memory, so the
+// addresses are looked up once per device (with that device current) and
+// cached.
+cudaError_t static_scratch(int device, void** out, unsigned long long** row_th) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_scratch_addr[device] == nullptr) {
         void* ptr = nullptr;
-        void* eptr = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-        if (e == cudaSuccess) e = cudaGetSymbolAddress(&eptr, g_static_err);
         void* rptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e == cudaSuccess) e = cudaGetSymbolAddress(&rptr, g_static_row_th);
-        g_row_th_addr[device] = rptr;
         if (e != cudaSuccess) return e;
+        g_row_th_addr[device] = rptr;
         g_scratch_addr[device] = ptr;
-        g_err_addr[device] = eptr;
     }
     *out = g_scratch_addr[device];
-    *err = static_cast<uint32_t*>(g_err_addr[device]);
-    if (++g_epoch[device] == 0u) g_epoch[device] = 1u;
-    *epoch = g_epoch[device];
+    *row_th = static_cast<unsigned long long*>(g_row_th_addr[device]);
     return cudaSuccess;
 }
 
@@ -100,9 +97,8 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
         return TQFS_ERR_NO_DEVICE;
     void* base = nullptr;
-    uint32_t* err = nullptr;
-    uint32_t epoch = 0;
-    if (static_scratch(device, &base, &err, &epoch) != cudaSuccess) return TQFS_ERR_CUDA;
+    unsigned long long* row_th = nullptr;
+    if (static_scratch(device, &base, &row_th) != cudaSuccess) return TQFS_ERR_CUDA;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     SampleArgs a{};
@@ -119,16 +115,14 @@ extern "C" int tqfs_sample_static(const void* logits_dev, int dtype, int rows, i
     a.out_token = out_token_dev;
     a.out_status = out_status_dev;
     stream_scratch(rows, plan, base, &a);
-    a.err_word = err;
-    a.row_th = static_cast<unsigned long long*>(g_row_th_addr[device]);
-    a.epoch = epoch;
+    a.row_th = row_th;
     const size_t esz = dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = (reinterpret_cast<uintptr_t>(logits_dev) & 15u) == 0 &&
                (static_cast<size_t>(ld) * esz) % 16 == 0;
     a.top4_only = 0;
     a.vocab_route = vocab;
 
-    mark_unhandled_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token_dev, out_status_dev);
+    mark_unhandled_kernel<<<(rows + 255) / 256, 256, 0, s>>>(rows, out_token_dev, out_status_dev, row_th);
     if (cudaGetLastError() != cudaSuccess) return TQFS_ERR_CUDA;
     if (launch_window(a, plan, s) != cudaSuccess) return TQFS_ERR_CUDA;
     const bool window = hist_off_dev != nullptr;

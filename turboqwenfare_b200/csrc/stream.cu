@@ -29,16 +29,30 @@
 //        bisection over the order values, keeping the count >= k; exact ties
 //        at the final value are resolved to the lowest ids.
 //
-// Finalising: the warp that completes a row's last unit (per-row tickets)
-//   takes the union of the units' lists. Every unit's k-th value is a lower
-//   bound of the row's k-th value, so the largest of them filters the lists;
-//   the survivors' exact top-k is ranked, and softmax, top_p, min_p and the
-//   inverse-CDF draw run over it exactly as src/sampling/mod.rs:166-248 does
-//   (sequential f32 sums in order, by one lane).
+// finalize_kernel: launched behind the stream grid (programmatic stream
+//   serialisation), one warp per row once the whole grid has written its
+//   unit lists. Greedy rows take the top-4 of the units' top-4 lists; sampled
+//   rows take the union of the units' lists (every unit k-th value is a lower
+//   bound of the row's k-th value, so the largest of them filters the
+//   lists), rank its exact top-k, and run softmax, top_p, min_p and the
+//   inverse-CDF draw exactly as src/sampling/mod.rs:166-248 does (sequential
+//   f32 sums in order, by one lane).
 //
-// No warp waits on another warp or CTA. The only waits are on a
-// warp's own bulk copies; each gives up after 2 s, sets the call's error word
-// and the rows report TQFS_ROW_ERR_TIMEOUT.
+// Per-call state. Besides scratch that each call writes before reading, a
+// row has one 64-bit word (SampleArgs::row_th): the largest k-th bound any
+// unit of the row published this call (atomicMax, low 32 bits) and
+// kRowFailed when one of the row's copy waits gave up. The word is zero when
+// a call starts: the finalize kernel reads and clears it, in stream order,
+// so a call replayed from a captured graph or a buffer reused by another
+// handle starts clean.
+//
+// Waits. No warp waits on another warp or CTA; the only waits are on a
+// warp's own bulk copies, each bounded (SampleArgs::wait_ns, 2 s by
+// default). A wait that gives up marks the row it was copying and every row
+// the warp would handle afterwards with kRowFailed (those rows report
+// TQFS_ROW_ERR_TIMEOUT, token -1), and the warp stops issuing copies. Before
+// the CTA exits, the warp waits (bounded again) for every copy it issued, so
+// no asynchronous write lands in shared memory after the CTA has gone.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -68,7 +82,6 @@ constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
 constexpr int kWinWarps = 16;     // warps of the window kernel
 constexpr int kFinWarps = 4;      // warps (rows) per CTA of the finalize kernel
 constexpr int kFinWarpSmem = kListCap * 8 + kStreamMaxK * 8 + 256 * 4;
-constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s per copy wait
 
 __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned long long k) {
     if (k <= t[3]) return;
@@ -1045,6 +1058,7 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int nw = static_cast<int>(gridDim.x) * kSW;
     const int nw_row = nw % a.rows, nw_u = nw / a.rows;
+    const unsigned long long budget = a.wait_ns != 0ull ? a.wait_ns : kDefaultWaitNs;
     const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
 
     auto chunk_len = [&](const Info& f) {
@@ -1054,6 +1068,10 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
     // Buffer bi receives the item's chunk: one bulk copy of its 16-byte
     // multiple (lane 0), plain copies of anything else (unaligned rows or a
     // ragged tail). Every item, copied or not, completes one barrier phase.
+    // `issued` bit bi: a bulk copy into buffer bi is in flight. With the
+    // stall test hook, a row's copies are armed on the barrier but never
+    // issued, so the waits for them run out and nothing is in flight.
+    uint32_t issued = 0u;
     auto start_copy = [&](const Info& f, int bi) {
         unsigned char* buf = wbase + bi * Raw<DT>::kBuf;
         const bool copy = f.mode == kModeGreedy || f.mode == kModeStream;
@@ -1066,10 +1084,12 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
             bytes = chunk_len(f) * ES;
             bulk = a.vec_ok ? static_cast<uint32_t>(bytes) & ~15u : 0u;
         }
+        const bool stall = copy && f.row + 1 == a.stall_row_p1;
+        if (bulk != 0u && !stall) issued |= 1u << bi;
         if (lane == 0) {
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&wbar[warp][bi], bulk);
-            if (bulk != 0u) bulk_load(buf, src, bulk, &wbar[warp][bi]);
+            if (bulk != 0u && !stall) bulk_load(buf, src, bulk, &wbar[warp][bi]);
         }
         for (int i = static_cast<int>(bulk) / ES + lane; i < bytes / ES; i += 32) {
             if constexpr (DT == 0)
@@ -1131,19 +1151,21 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
         const unsigned long long rb =
             (sel && a.row_th != nullptr && cur.mode == kModeStream) ? __ldcg(a.row_th + cur.row) : 0ull;
         if (!failed) {
-            const bool ok = mbar_wait_bounded(&wbar[warp][b], (parity >> b) & 1u, kWaitBudgetNs);
-            parity ^= 1u << b;
-            if (!__all_sync(0xFFFFFFFFu, ok)) {
-                // A copy did not land in time: report it, wait (bounded) for
-                // the other buffer's copy, and from here on only count this
-                // warp's units so their rows still report.
+            const bool ok = mbar_wait_bounded(&wbar[warp][b], (parity >> b) & 1u, budget);
+            if (__all_sync(0xFFFFFFFFu, ok)) {
+                parity ^= 1u << b;
+                issued &= ~(1u << b);
+            } else {
+                // A copy did not land in time: issue nothing more. This row
+                // and every row this warp would handle from here on report
+                // the timeout; the copies still in flight are waited for
+                // before the CTA exits.
                 failed = true;
-                if (lane == 0) {
-                    atomicMax(a.err_word, a.epoch);
-                    mbar_wait_bounded(&wbar[warp][b ^ 1], (parity >> (b ^ 1)) & 1u, kWaitBudgetNs);
-                }
             }
         }
+        if (failed && lane == 0 && a.row_th != nullptr &&
+            (cur.mode == kModeGreedy || cur.mode == kModeStream))
+            atomicOr(a.row_th + cur.row, kRowFailed);
         __syncwarp();
 
         if (!failed && (cur.mode == kModeGreedy || cur.mode == kModeStream)) {
@@ -1225,7 +1247,7 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                 float th = sel ? from_order32(th_ord) : 0.0f;
                 bool incl_sel = false;
                 if (sel) {
-                    const uint32_t fo = (rb >> 32) == a.epoch ? static_cast<uint32_t>(rb) : 0u;
+                    const uint32_t fo = static_cast<uint32_t>(rb);
                     if (fo > th_ord) {
                         th = from_order32(fo);
                         incl_sel = true;
@@ -1254,7 +1276,7 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                     th_ord = static_cast<uint32_t>(kth >> 32);
                     sel = n >= k && th_ord != 0u;  // a NaN k-th admits every number
                     if (sel && lane == 0 && a.row_th != nullptr)
-                        atomicMax(a.row_th + cur.row, (static_cast<unsigned long long>(a.epoch) << 32) | th_ord);
+                        atomicMax(a.row_th + cur.row, static_cast<unsigned long long>(th_ord));
                 }
                 // ---- 6. unit end: its exact top-k and its k-th value -------
                 if (cur.last) {
@@ -1284,6 +1306,14 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
         nxt = nn;
         b ^= 1;
     }
+    // After a timeout: wait (bounded) for the copies this warp issued, so none
+    // lands in shared memory the next CTA on this SM may own.
+    if (failed && lane == 0) {
+#pragma unroll
+        for (int bi = 0; bi < 2; ++bi)
+            if (issued & (1u << bi)) mbar_wait_bounded(&wbar[warp][bi], (parity >> bi) & 1u, budget);
+    }
+    __syncwarp();
 }
 
 // Finalises the rows the stream kernel owns, one warp per row, once every unit
@@ -1312,7 +1342,16 @@ __global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(SampleArgs a) 
     const bool lists = !a.top4_only && lane < a.units;
     const int m_raw = lists ? __ldcg(a.cand_n + base + lane) : 0;
     const uint32_t th_u = lists ? __ldcg(a.theta + base + lane) : 0u;
-    const bool timed_out = *reinterpret_cast<volatile uint32_t*>(a.err_word) == a.epoch;
+    // The row's per-call word: read, then cleared for the next call.
+    unsigned long long rw = 0ull;
+    if (a.row_th != nullptr) {
+        if (lane == 0) {
+            rw = __ldcg(a.row_th + row);
+            a.row_th[row] = 0ull;
+        }
+        rw = __shfl_sync(0xFFFFFFFFu, rw, 0);
+    }
+    const bool timed_out = (rw & kRowFailed) != 0ull;
     const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
     if (mode != kModeGreedy && mode != kModeStream) return;
     finalize_row(a, row, mode == kModeGreedy, static_cast<int>(p.top_k), p, mode == kModeGreedy ? 0 : m_raw,
@@ -1444,6 +1483,20 @@ int sm_count() {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Sets a kernel's dynamic shared memory limit once per device (per host
+// thread): bit d of *mask records device d.
+template <typename K>
+cudaError_t set_smem_once(K kern, int bytes, unsigned long long* mask) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (bit != 0ull && (*mask & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) *mask |= bit;
+    return e;
+}
+
 constexpr size_t kWindowSmem = static_cast<size_t>(2 * (kMaxChunks + 1)) * 4 +
                                static_cast<size_t>(kWinWarps) * (kChunkLen / 2) * 4 +
                                static_cast<size_t>(kWinCap) * 2;
@@ -1523,8 +1576,8 @@ SampleArgs with_plan(const SampleArgs& a_in, const Plan& plan) {
 cudaError_t launch_window(const SampleArgs& a_in, const Plan& plan, cudaStream_t s) {
     if (a_in.rows <= 0 || plan.units <= 0 || a_in.hist_off == nullptr || a_in.top4_only) return cudaSuccess;
     const SampleArgs a = with_plan(a_in, plan);
-    cudaError_t e = cudaFuncSetAttribute(window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kWindowSmem));
+    static thread_local unsigned long long done = 0ull;
+    const cudaError_t e = set_smem_once(window_kernel, static_cast<int>(kWindowSmem), &done);
     if (e != cudaSuccess) return e;
     window_kernel<<<a.rows, kWinWarps * 32, kWindowSmem, s>>>(a);
     return cudaGetLastError();
@@ -1536,8 +1589,8 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     const SampleArgs a = with_plan(a_in, plan);
     void (*kern)(SampleArgs, int) =
         a.dtype == TQFS_DTYPE_F32 ? stream_kernel<0> : stream_kernel<1>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(plan.smem));
+    static thread_local unsigned long long done[2] = {0ull, 0ull};
+    const cudaError_t e = set_smem_once(kern, static_cast<int>(plan.smem), &done[a.dtype == TQFS_DTYPE_F32 ? 0 : 1]);
     if (e != cudaSuccess) return e;
     // Every SM gets a CTA (warps are numbered across CTAs first, so the units
     // spread over all SMs even when there are fewer units than warps).
@@ -1561,15 +1614,9 @@ cudaError_t launch_finalize(const SampleArgs& a_in, const Plan& plan, cudaStream
     if (a_in.rows <= 0 || plan.units <= 0) return cudaSuccess;
     const SampleArgs a = with_plan(a_in, plan);
     const int fin_smem = kFinWarps * kFinWarpSmem;
-    static thread_local int fin_configured = -1;  // the device whose attribute is set
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static thread_local unsigned long long done = 0ull;
+    const cudaError_t e = set_smem_once(finalize_kernel, fin_smem, &done);
     if (e != cudaSuccess) return e;
-    if (fin_configured != dev) {
-        e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem);
-        if (e != cudaSuccess) return e;
-        fin_configured = dev;
-    }
     cudaLaunchConfig_t fc = {};
     fc.gridDim = dim3(static_cast<unsigned>((a.rows + kFinWarps - 1) / kFinWarps));
     fc.blockDim = dim3(kFinWarps * 32);
@@ -1586,8 +1633,8 @@ cudaError_t launch_finalize(const SampleArgs& a_in, const Plan& plan, cudaStream
 cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s) {
     if (m.rows <= 0) return cudaSuccess;
     const size_t smem = static_cast<size_t>(kSW) * kMergeSmem;
-    cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    static thread_local unsigned long long done = 0ull;
+    const cudaError_t e = set_smem_once(merge_kernel, static_cast<int>(smem), &done);
     if (e != cudaSuccess) return e;
     const int ctas = (m.rows + kSW - 1) / kSW;
     merge_kernel<<<ctas, kSW * 32, smem, s>>>(m);
