@@ -103,9 +103,10 @@ const char* tqfs_last_error(const tqfs_handle* handle);
 /* Accumulated device time of the library's kernels since the last reset,
  * measured with CUDA events on the launching stream when timing is enabled
  * (the events also keep consecutive kernels from overlapping). kernel_ms[i]
- * and launches[i] are filled for i < n, i = 0: stream kernel, 1: general
- * kernel, 2: window pre-pass, 3: MTP verify, 4: the stream rows' finalize
- * kernel. Test and benchmark instrumentation only. */
+ * and launches[i] are filled for i < n, i = 0: stream kernel (which also
+ * finalises its rows), 1: general kernel (or the shard merge), 2: window
+ * pre-pass, 3: MTP verify, 4: unused (always 0). Test and benchmark
+ * instrumentation only. */
 int tqfs_set_timing(tqfs_handle* handle, int enabled);
 int tqfs_get_timing(tqfs_handle* handle, int n, float* kernel_ms, int64_t* launches);
 /* How the stream kernel splits a batch on the current device: each logits

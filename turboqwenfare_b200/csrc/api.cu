@@ -48,18 +48,18 @@ struct TimedLaunch {
 
 }  // namespace
 
-constexpr int kTimingKinds = 5;  // stream, general, window, MTP, finalize
+constexpr int kTimingKinds = 5;  // stream, general, window, MTP, (unused: rows finalise in the stream kernel)
 
 struct tqfs_handle {
     int device = 0;
     std::string error;
     DeviceBuffer scratch;      // candidate lists, counts, greedy lists
     DeviceBuffer general;      // general-kernel working arrays (counts kept zero)
-    DeviceBuffer row_th;       // per-row word of a call (bound, timeout); zero between calls
+    DeviceBuffer row_th;       // per-row words of a call (bound and timeout, unit tickets); zero between calls
     DeviceBuffer mtp;          // MTP verify workspaces
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
-    bool row_th_dirty = false; // a call launched the stream kernel but not its finalize
+    bool row_th_dirty = false; // a call's stream kernel failed to launch after its window pre-pass
     int stall_row_p1 = 0;      // test hook for the next call (tqfs_debug_stall_row)
     unsigned long long stall_wait_ns = 0;
     size_t general_layout[3] = {0, 0, 0};
@@ -157,16 +157,16 @@ int ensure_current(tqfs_handle* h) {
 
 // Scratch of the stream path (candidate lists, chunk bounds, greedy lists,
 // window buckets), grown on demand; every field a kernel reads is written
-// earlier in the same call. The per-row words (row_th) must be zero when a
-// call starts: new memory is zeroed on the call's stream, and every call's
-// finalize kernel clears the words it read.
+// earlier in the same call. The per-row words (bound/timeout and unit
+// tickets) must be zero when a call starts: new memory is zeroed on the
+// call's stream, and the warp that finalises a row zeroes its words.
 int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::SampleArgs& a,
                    cudaStream_t s) {
     const size_t bytes = tqfs::stream_scratch(rows, plan, nullptr, nullptr);
     cudaError_t e = h->scratch.reserve(bytes);
     if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
     tqfs::stream_scratch(rows, plan, h->scratch.ptr, &a);
-    const size_t words = static_cast<size_t>(rows) * 8;
+    const size_t words = static_cast<size_t>(rows) * 12;  // u64 bound word + u32 ticket per row
     if (h->row_th.bytes < words || h->row_th_dirty) {
         e = h->row_th.reserve(words);
         if (e == cudaSuccess) e = cudaMemsetAsync(h->row_th.ptr, 0, h->row_th.bytes, s);
@@ -174,6 +174,7 @@ int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::Sampl
         h->row_th_dirty = false;
     }
     a.row_th = static_cast<unsigned long long*>(h->row_th.ptr);
+    a.row_tk = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(h->row_th.ptr) + static_cast<size_t>(rows) * 8);
     a.wait_ns = h->stall_wait_ns;       // 0: the kernels' default budget
     a.stall_row_p1 = h->stall_row_p1;   // the test hook lasts one call
     h->stall_wait_ns = 0;
@@ -181,9 +182,9 @@ int ensure_scratch(tqfs_handle* h, int rows, const tqfs::Plan& plan, tqfs::Sampl
     return TQFS_OK;
 }
 
-// Launches the window pre-pass, the stream kernel and its finalize kernel.
-// A finalize that fails to launch after the stream kernel did leaves per-row
-// words set; the next call then zeroes them first.
+// Launches the window pre-pass and the stream kernel (which finalises its
+// rows). If the stream kernel fails to launch after the pre-pass did, the
+// next call zeroes the per-row words first.
 cudaError_t launch_stream_path(tqfs_handle* h, const tqfs::SampleArgs& a, const tqfs::Plan& plan,
                                cudaStream_t s, bool window) {
     cudaError_t e;
@@ -195,11 +196,6 @@ cudaError_t launch_stream_path(tqfs_handle* h, const tqfs::SampleArgs& a, const 
     {
         TimingScope ts(h, s, 0);
         e = tqfs::launch_stream(a, plan, s, window && !h->timing);
-    }
-    if (e != cudaSuccess) return e;
-    {
-        TimingScope ts(h, s, 4);
-        e = tqfs::launch_finalize(a, plan, s, !h->timing);
     }
     if (e != cudaSuccess) h->row_th_dirty = true;
     return e;

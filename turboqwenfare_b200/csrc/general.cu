@@ -179,8 +179,8 @@ cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int cta
         configured = dev;
     }
     // General rows read only the call's inputs, so with `overlap` the kernel
-    // may start while the kernel in front of it (the stream rows' finalize,
-    // which writes other rows) still runs.
+    // may start while the kernel in front of it (the stream kernel, which
+    // writes other rows) still runs.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(ctas));
     cfg.blockDim = dim3(kGenThreads);

@@ -41,6 +41,9 @@ struct SampleArgs {
     // and kRowFailed when a copy wait of the row gave up. Zero when a call
     // starts: the finalize kernel clears each row's word after reading it.
     unsigned long long* row_th;
+    // rows: units of the row that have finished; the warp that finishes the
+    // last one finalises the row and zeroes both per-row words.
+    uint32_t* row_tk;
     unsigned long long wait_ns;  // budget of each bounded copy wait (0: kDefaultWaitNs)
     int stall_row_p1;          // test hook: 1 + the row whose copies are armed but never
                                // issued, so its waits run out (0: none)
@@ -118,13 +121,11 @@ Plan plan_stream(int rows, int vocab, int dtype);
 // Bytes of stream-path scratch for `rows`; with a non-null base, also points
 // a's scratch fields into [base, base + bytes).
 size_t stream_scratch(int rows, const Plan& plan, void* base, SampleArgs* a);
-// The window pre-pass (a no-op without a history), then the stream kernel;
-// after_window lets the stream kernel's launch overlap the pre-pass.
+// The window pre-pass (a no-op without a history), then the stream kernel,
+// which also finalises its rows; after_window lets the stream kernel's
+// launch overlap the pre-pass.
 cudaError_t launch_window(const SampleArgs& a, const Plan& plan, cudaStream_t s);
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool after_window);
-// Finalises the stream kernel's rows (one warp per row); `overlap` launches it
-// behind the stream grid (programmatic serialization).
-cudaError_t launch_finalize(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool overlap);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
 cudaError_t launch_general(const SampleArgs& a, const GeneralScratch& g, int ctas, cudaStream_t s,
                            bool overlap);

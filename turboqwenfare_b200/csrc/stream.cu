@@ -29,22 +29,25 @@
 //        bisection over the order values, keeping the count >= k; exact ties
 //        at the final value are resolved to the lowest ids.
 //
-// finalize_kernel: launched behind the stream grid (programmatic stream
-//   serialisation), one warp per row once the whole grid has written its
-//   unit lists. Greedy rows take the top-4 of the units' top-4 lists; sampled
-//   rows take the union of the units' lists (every unit k-th value is a lower
-//   bound of the row's k-th value, so the largest of them filters the
-//   lists), rank its exact top-k, and run softmax, top_p, min_p and the
-//   inverse-CDF draw exactly as src/sampling/mod.rs:166-248 does (sequential
-//   f32 sums in order, by one lane).
+// Finalising: every unit writes its exact top-k (k <= 32: sorted) and takes
+//   a per-row ticket; the warp taking the row's last ticket finalises the
+//   row in the same kernel. Greedy rows take the top-4 of the units' top-4
+//   lists; sampled rows with k <= 32 merge the units' sorted lists (the
+//   union holds the row's top-k) with register bitonic merges, larger k
+//   gather the lists filtered by the largest unit k-th value and rank them.
+//   Softmax, top_p, min_p and the inverse-CDF draw then run exactly as
+//   src/sampling/mod.rs:166-248 does (the same sequential f32 sums, in
+//   order). Measured on c1x256, finalising in a separate kernel behind the
+//   grid cost 17 us of one-warp-per-row latency after the grid had drained.
 //
 // Per-call state. Besides scratch that each call writes before reading, a
-// row has one 64-bit word (SampleArgs::row_th): the largest k-th bound any
-// unit of the row published this call (atomicMax, low 32 bits) and
-// kRowFailed when one of the row's copy waits gave up. The word is zero when
-// a call starts: the finalize kernel reads and clears it, in stream order,
-// so a call replayed from a captured graph or a buffer reused by another
-// handle starts clean.
+// row has a 64-bit word (SampleArgs::row_th: the largest k-th bound any unit
+// of the row published this call, atomicMax on the low 32 bits, and
+// kRowFailed when one of the row's copy waits gave up) and a ticket count
+// (SampleArgs::row_tk). Both are zero when a call starts: the warp that
+// finalises the row reads and zeroes them, in stream order, so a call
+// replayed from a captured graph or a buffer reused by another handle
+// starts clean.
 //
 // Waits. No warp waits on another warp or CTA; the only waits are on a
 // warp's own bulk copies, each bounded (SampleArgs::wait_ns, 2 s by
@@ -64,24 +67,14 @@ namespace tqfs {
 
 namespace {
 
-constexpr int kSW = 11;           // warps per CTA of the stream kernel
-// Registers: 11 warps fit an SM at 168 registers a thread (3 warps on three
-// schedulers, 2 on the fourth, 16,128 of 16,384 registers each); the launch
-// bound of 384 threads makes the compiler hold to that.
-constexpr int kStreamBound = 384;
-constexpr int kST = kSW * 32;
+constexpr int kSW = 11;           // warps per CTA of the merge kernel
 constexpr int kSlots = 16;        // float4 register slots per lane per chunk
 constexpr int kChunkLen = kSlots * 32 * 4;  // 2,048 ids per chunk
 constexpr int kListCap = 384;     // keys of a warp's candidate list
-constexpr int kListOff = 16384;   // per-warp shared memory: chunk buffers (+ exchange),
-constexpr int kBinsOff = kListOff + kListCap * 8;  // candidate list, digit bins
-constexpr int kWarpSmem = kBinsOff + 256 * 4;      // 20 KiB: 11 warps in 220 KiB
 constexpr int kMaxUnits = 32;                      // units per row (one lane each)
 constexpr int kMergeSmem = kListCap * 8 + 1024 + kStreamMaxK * 8;  // per merge warp
 constexpr int kUnitCap = kStreamMaxK;              // keys a unit writes
 constexpr int kWinWarps = 16;     // warps of the window kernel
-constexpr int kFinWarps = 4;      // warps (rows) per CTA of the finalize kernel
-constexpr int kFinWarpSmem = kListCap * 8 + kStreamMaxK * 8 + 256 * 4;
 
 __device__ __forceinline__ void top4_insert(unsigned long long t[4], unsigned long long k) {
     if (k <= t[3]) return;
@@ -199,6 +192,38 @@ struct Raw {
     static constexpr int kES = DT == 0 ? 4 : 2;   // element bytes
     static constexpr int kBuf = kChunkLen * kES;  // bytes of a chunk buffer
 };
+
+// Per-warp shared memory of the stream kernel and warps per CTA, by logits
+// type: kNB chunk buffers (kNB - 1 copies in flight while the warp works on
+// one), for bf16 an 8 KiB f32 exchange area for penalised chunks, then the
+// candidate list (kListCap keys) and 256 digit bins. The per-chunk selection
+// is latency-bound, so warps per SM count for more than buffer depth: both
+// types run 11 warps (168 registers a thread under the 384-thread launch
+// bound: three warps on three schedulers, two on the fourth) with two
+// buffers. Measured on c1x256, 8 warps with three f32 buffers ran the stream
+// kernel at 61 us against 49 us.
+template <int DT> struct StreamLayout;
+template <> struct StreamLayout<0> {
+    static constexpr int kWarps = 11, kNB = 2, kXch = 0, kBound = 384;
+};
+template <> struct StreamLayout<1> {
+    static constexpr int kWarps = 11, kNB = 2, kXch = 8192, kBound = 384;
+};
+template <int DT>
+struct SL : StreamLayout<DT> {
+    static constexpr int kListOff = StreamLayout<DT>::kNB * Raw<DT>::kBuf + StreamLayout<DT>::kXch;
+    static constexpr int kBinsOff = kListOff + kListCap * 8;
+    static constexpr int kWarpSmem = kBinsOff + 256 * 4;
+    static constexpr int kSmem = StreamLayout<DT>::kWarps * kWarpSmem;
+};
+static_assert(SL<0>::kSmem <= 227 * 1024 - 512 && SL<1>::kSmem <= 227 * 1024 - 512, "stream smem");
+
+// max of three floats, NaN operands ignored (max.f32 with three inputs).
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(x), "f"(y), "f"(z));
+    return d;
+}
 
 struct Pen {
     float rep, freq, pres;
@@ -570,7 +595,7 @@ __device__ __forceinline__ void slot_maxima(const void* vals, int n_here, int la
 #pragma unroll
             for (int j = 0; j < kSlots; ++j) {
                 const float4 v = p[j * 32 + lane];
-                sm[j] = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+                sm[j] = fmax3(fmaxf(v.x, v.y), v.z, v.w);
             }
         } else {
             const uint4* p = static_cast<const uint4*>(vals);
@@ -664,6 +689,14 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
         if (!(thr > -INFINITY)) return -1;  // too few numbers: select in full
     }
     const bool incl = !sel || incl_sel;
+    if (sel) {
+        // Fast path: when no lane's maximum passes th, nothing in the chunk does.
+        const float m0 = fmax3(sm[0], sm[1], sm[2]), m1 = fmax3(sm[3], sm[4], sm[5]);
+        const float m2 = fmax3(sm[6], sm[7], sm[8]), m3 = fmax3(sm[9], sm[10], sm[11]);
+        const float m4 = fmax3(sm[12], sm[13], sm[14]);
+        const float lm = fmax3(fmax3(m0, m1, m2), fmax3(m3, m4, sm[15]), -INFINITY);
+        if (!__any_sync(0xFFFFFFFFu, incl ? lm >= thr : lm > thr)) return 0;
+    }
     unsigned mask = 0u;
 #pragma unroll
     for (int j = 0; j < kSlots; ++j)
@@ -852,6 +885,139 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
     return token;
 }
 
+// Top 32 of two lists sorted descending across the warp (one key a lane),
+// sorted descending: the max of one list and the other reversed is bitonic
+// and holds the top 32 of the union; five half-cleaner stages sort it.
+__device__ __forceinline__ unsigned long long merge_top32(unsigned long long x, unsigned long long y,
+                                                          int lane) {
+    const unsigned long long yr = __shfl_sync(0xFFFFFFFFu, y, 31 - lane);
+    unsigned long long c = umax64(x, yr);
+#pragma unroll
+    for (int st = 16; st > 0; st >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, c, st);
+        c = (lane & st) == 0 ? umax64(c, o) : umin64(c, o);
+    }
+    return c;
+}
+
+// Lane i's value of the sequential f32 sum init + x_0 + ... + x_i over the
+// lanes' x (lanes < n), evaluated in that order by every lane (the same
+// additions, in the same order, as one running sum: each lane keeps its own
+// prefix), so a cut or a draw becomes a ballot over the prefixes.
+__device__ __forceinline__ float seq_prefix(float x, int n, float init, int lane) {
+    float c = init, mine = init;
+    for (int j = 0; j < n; ++j) {
+        c = __fadd_rn(c, __shfl_sync(0xFFFFFFFFu, x, j));
+        if (j == lane) mine = c;
+    }
+    return mine;
+}
+
+// src/sampling/mod.rs:166-248 over a row's top-k (k <= 32) held one key a
+// lane, sorted descending (lanes >= kk hold 0): softmax, top_p, min_p and the
+// inverse-CDF draw with exactly the reference's f32 operations. Every
+// sequential sum is a seq_prefix (all lanes, same order), so the cuts and
+// the draw are ballots. Returns the token (every lane); with out_probs_row,
+// writes the kept probabilities at their tokens.
+__device__ __noinline__ int finish_sampled_lanes(const tqfs_params& p, unsigned long long key, int kk,
+                                                 const float* uniforms, uint64_t* rng_state, int row,
+                                                 float* out_probs_row) {
+    const int lane = threadIdx.x & 31;
+    float u_in = 0.0f;
+    uint64_t st[4] = {0ull, 0ull, 0ull, 0ull};
+    if (lane == 0) {
+        if (uniforms != nullptr) {
+            u_in = __ldg(uniforms + row);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st[q] = rng_state[static_cast<size_t>(row) * 4 + q];
+        }
+    }
+    const bool in = lane < kk;
+    const float v = key_value(key);
+    const float first = __shfl_sync(0xFFFFFFFFu, v, 0);
+    const float mx = (kk > 0 && first == first) ? first : -INFINITY;
+    const float e = in ? exp_f32(__fdiv_rn(__fsub_rn(v, mx), p.temperature)) : 0.0f;
+    const float total_e = __shfl_sync(0xFFFFFFFFu, seq_prefix(e, kk, -0.0f, lane), kk > 0 ? kk - 1 : 0);
+    float pr = total_e > 0.0f ? __fdiv_rn(e, total_e) : e;
+    uint32_t tok = key_token(key);
+    // Draw order (p desc, id asc): the value order except where distinct
+    // values share a p (or a p is NaN); only then are probability keys sorted.
+    const float pn = __shfl_down_sync(0xFFFFFFFFu, pr, 1);
+    const float vn = __shfl_down_sync(0xFFFFFFFFu, v, 1);
+    const bool re = in && (pr != pr || (lane + 1 < kk && pn == pr && vn != v));
+    if (__any_sync(0xFFFFFFFFu, re)) {
+        const unsigned long long pk = warp_sort_desc(in ? make_key(order32(pr), tok) : 0ull, lane);
+        pr = key_value(pk);
+        tok = key_token(pk);
+    }
+    // top_p (mod.rs:195-209): the shortest prefix whose running sum reaches it
+    const float cum = seq_prefix(in ? pr : 0.0f, kk, 0.0f, lane);
+    int keep = kk;
+    if (!(p.top_p >= 1.0f)) {
+        const unsigned b = __ballot_sync(0xFFFFFFFFu, in && cum >= p.top_p);
+        keep = b ? __ffs(b) : kk;
+        keep = keep < 1 ? 1 : keep;
+        keep = keep > kk ? kk : keep;
+    }
+    // min_p (mod.rs:213-224): the prefix with p >= min_p * p[0], at least one
+    if ((p.flags & TQFS_PARAM_HAS_MIN_P) && !(p.min_p <= 0.0f) && keep > 0) {
+        const float floor = __fmul_rn(p.min_p, __shfl_sync(0xFFFFFFFFu, pr, 0));
+        const unsigned b = __ballot_sync(0xFFFFFFFFu, lane < keep && !(pr >= floor));
+        const int c = b ? __ffs(b) - 1 : keep;
+        keep = c < 1 ? 1 : c;
+    }
+    // draw (mod.rs:227-248): total over the kept prefix, then the first
+    // running sum reaching u * total
+    int pick = 0;
+    if (keep > 0) {
+        const float total2 = __shfl_sync(0xFFFFFFFFu, cum, keep - 1);
+        if (isfinite(total2) && total2 > 0.0f) {
+            float u = u_in;
+            if (uniforms == nullptr && lane == 0) {
+                u = xoshiro_next_f32(st);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) rng_state[static_cast<size_t>(row) * 4 + q] = st[q];
+            }
+            const float target = __fmul_rn(__shfl_sync(0xFFFFFFFFu, u, 0), total2);
+            const unsigned b = __ballot_sync(0xFFFFFFFFu, lane < keep && cum >= target);
+            pick = b ? __ffs(b) - 1 : keep - 1;
+        }
+    }
+    const int token = keep > 0 ? static_cast<int>(__shfl_sync(0xFFFFFFFFu, tok, pick)) : 0;
+    if (out_probs_row != nullptr && lane < keep) out_probs_row[tok] = pr;
+    __syncwarp();
+    return token;
+}
+
+// The row's exact top-k (k <= 32), sorted descending one key a lane, from
+// its units' sorted top-k lists (the union holds the row's top-k): the lists
+// are staged in shared memory in one batch of loads, then merged pairwise.
+// *kk gets min(k, keys available).
+__device__ __forceinline__ unsigned long long merge_unit_lists(const SampleArgs& a, int row, int k,
+                                                               unsigned long long* L, int* kk) {
+    const int lane = threadIdx.x & 31;
+    const int U = a.units;
+    const size_t base = static_cast<size_t>(row) * U;
+    const int m_own = lane < U ? min(max(__ldcg(a.cand_n + base + lane), 0), k) : 0;
+    int avail = warp_sum(m_own);
+    // units beyond the list area (never more than kListCap / 32) are merged as they load
+    unsigned long long acc = 0ull;
+    for (int u0 = 0; u0 < U; u0 += kListCap / 32) {
+        const int nu = min(U - u0, kListCap / 32);
+#pragma unroll 4
+        for (int j = 0; j < nu; ++j) {
+            const int m = __shfl_sync(0xFFFFFFFFu, m_own, u0 + j);
+            L[j * 32 + lane] = lane < m ? __ldcg(a.cand + (base + u0 + j) * kUnitCap + lane) : 0ull;
+        }
+        __syncwarp();
+        for (int j = 0; j < nu; ++j) acc = merge_top32(acc, L[j * 32 + lane], lane);
+        __syncwarp();
+    }
+    *kk = min(avail, k);
+    return lane < *kk ? acc : 0ull;
+}
+
 // Finalises a row in one warp once all its units have written their lists:
 // greedy rows take the top-4 (src/runtime/decode.rs:48-64); sampled rows the
 // union of the units' lists (every row top-k member is in its unit's top-k)
@@ -861,7 +1027,7 @@ __device__ __noinline__ int finish_sampled(const tqfs_params& p, int k, unsigned
 // The caller passes what it loaded in one trip: the row's parameters, lane
 // u's unit list length m_raw and bound th_u (sampled rows), and whether the
 // call timed out.
-__device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool greedy, int k,
+__device__ __forceinline__ void finalize_row(const SampleArgs& a, int row, bool greedy, int k,
                                           const tqfs_params& p, int m_raw, uint32_t th_u,
                                           bool timed_out, unsigned long long* L,
                                           unsigned long long* S, unsigned int* bins) {
@@ -907,7 +1073,21 @@ __device__ __noinline__ void finalize_row(const SampleArgs& a, int row, bool gre
         }
         token = o[0] ? static_cast<int>(key_token(o[0])) : 0;
     }
-    if (!greedy) {
+    if (!greedy && k <= 32) {
+        int kk = 0;
+        const unsigned long long key = merge_unit_lists(a, row, k, L, &kk);
+        if (rec != nullptr) {  // export: the shard's exact top-k, global ids
+            if (lane < kk) rec[2 + lane] = key - goff;
+            if (lane == 0) {
+                rec[0] = static_cast<unsigned long long>(kk);
+                rec[1] = 0ull;
+            }
+            __syncwarp();
+            return;
+        }
+        float* pr = a.out_probs != nullptr ? a.out_probs + static_cast<size_t>(row) * a.ld : nullptr;
+        token = finish_sampled_lanes(p, key, kk, a.uniforms, a.rng_state, row, pr);
+    } else if (!greedy) {
         // Lists: lane u holds unit u's length and bound (units <= 32); the
         // list offsets go to S until the survivors are ranked there.
         const int m_u = min(max(m_raw, 0), kUnitCap);
@@ -1029,23 +1209,61 @@ __global__ void __launch_bounds__(kSW * 32) merge_kernel(MergeArgs m) {
     }
 }
 
+// Finalises `row` in the calling warp once all its units have written their
+// lists: its parameters, its per-row word (timeout mark) and, for the
+// gather path (k > 32), the units' list lengths and bounds, loaded in one
+// trip; then the per-row words are zeroed for the next call. S takes up to
+// kStreamMaxK keys (a consumed chunk buffer), L kListCap keys, bins 256.
+__device__ __forceinline__ void finalize_in_stream(const SampleArgs& a, int row, unsigned long long* S,
+                                                unsigned long long* L, unsigned int* bins) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long w = 0ull;
+    if (lane < 10 && !a.top4_only) w = __ldg(reinterpret_cast<const unsigned int*>(a.params + row) + lane);
+    if (lane == 10) w = __ldcg(a.row_th + row);
+    if (lane == 11 && a.hist_off != nullptr) w = static_cast<unsigned long long>(__ldg(a.hist_off + row));
+    if (lane == 12 && a.hist_off != nullptr) w = static_cast<unsigned long long>(__ldg(a.hist_off + row + 1));
+    const size_t base = static_cast<size_t>(row) * a.units;
+    const bool lists = !a.top4_only && lane < a.units;
+    const int m_raw = lists ? __ldcg(a.cand_n + base + lane) : 0;
+    const uint32_t th_u = lists ? __ldcg(a.theta + base + lane) : 0u;
+    unsigned int pw[10];
+#pragma unroll
+    for (int i = 0; i < 10; ++i) pw[i] = static_cast<unsigned int>(__shfl_sync(0xFFFFFFFFu, w, i));
+    const unsigned long long rw = __shfl_sync(0xFFFFFFFFu, w, 10);
+    const long long hs = static_cast<long long>(__shfl_sync(0xFFFFFFFFu, w, 11));
+    const long long he = static_cast<long long>(__shfl_sync(0xFFFFFFFFu, w, 12));
+    if (lane == 0) {
+        a.row_th[row] = 0ull;
+        a.row_tk[row] = 0u;
+    }
+    tqfs_params p;
+    memcpy(&p, pw, sizeof(p));
+    long long ws, wl;
+    const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
+    const bool greedy = mode == kModeGreedy;
+    finalize_row(a, row, greedy, static_cast<int>(p.top_k), p, greedy ? 0 : m_raw, greedy ? 0u : th_u,
+                 (rw & kRowFailed) != 0ull, L, S, bins);
+}
+
 template <int DT>
-__global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, int top4_diag) {
+__global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a, int top4_diag) {
     constexpr int ES = Raw<DT>::kES;
+    constexpr int kWarps = SL<DT>::kWarps;
+    constexpr int kNB = SL<DT>::kNB;
     extern __shared__ __align__(16) unsigned char dyn[];
-    __shared__ int wcount[kSW];
-    __shared__ __align__(8) unsigned long long wbar[kSW][2];
+    __shared__ int wcount[kWarps];
+    __shared__ __align__(8) unsigned long long wbar[kWarps][kNB];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    // This warp's area: two chunk buffers, for bf16 an f32 exchange area (f32
-    // chunks are penalised in their own buffer), the candidate list, bins.
-    unsigned char* wbase = dyn + static_cast<size_t>(warp) * kWarpSmem;
-    float* xch = reinterpret_cast<float*>(wbase + 2 * Raw<DT>::kBuf);
-    unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase + kListOff);
-    unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + kBinsOff);
+    // This warp's area: kNB chunk buffers, for bf16 an f32 exchange area
+    // (f32 chunks are penalised in their own buffer), the candidate list, bins.
+    unsigned char* wbase = dyn + static_cast<size_t>(warp) * SL<DT>::kWarpSmem;
+    float* xch = reinterpret_cast<float*>(wbase + kNB * Raw<DT>::kBuf);
+    unsigned long long* L = reinterpret_cast<unsigned long long*>(wbase + SL<DT>::kListOff);
+    unsigned int* bins = reinterpret_cast<unsigned int*>(wbase + SL<DT>::kBinsOff);
     if (lane == 0) {
-        mbar_init(&wbar[warp][0], 1);
-        mbar_init(&wbar[warp][1], 1);
+#pragma unroll
+        for (int i = 0; i < kNB; ++i) mbar_init(&wbar[warp][i], 1);
         fence_mbar_init();
     }
     __syncwarp();
@@ -1053,10 +1271,10 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
     // Launched right behind the window kernel: wait for its buckets (a no-op
     // when there is no window kernel in front).
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // The finalize kernel behind this one may launch now (its CTAs find room
-    // as this grid's CTAs exit, and wait for the whole grid before reading).
+    // The kernel behind this one (general rows, which read only the call's
+    // inputs) may launch now; its CTAs find room as this grid's CTAs exit.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int nw = static_cast<int>(gridDim.x) * kSW;
+    const int nw = static_cast<int>(gridDim.x) * kWarps;
     const int nw_row = nw % a.rows, nw_u = nw / a.rows;
     const unsigned long long budget = a.wait_ns != 0ull ? a.wait_ns : kDefaultWaitNs;
     const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
@@ -1110,24 +1328,31 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
     };
 
     // Warps are numbered across CTAs first, so consecutive units land on
-    // different SMs. Prologue: positions p0 (cur) and p1 (nxt) are being
-    // copied; the words of p2 are in flight.
+    // different SMs. Prologue: the warp's first kNB positions q[0..kNB) are
+    // being copied into buffers 0..kNB-1; the words of position pn are in
+    // flight. q[i] sits in buffer (b + i) % kNB.
     const int gw = warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
-    Pos p0;
-    p0.row = gw % a.rows;
-    p0.u = gw / a.rows;
-    p0.chunk = p0.u * a.unit_len;
-    const Pos p1 = next_pos(a, p0, nw_row, nw_u);
-    Pos p2 = next_pos(a, p1, nw_row, nw_u);
-    Info none;
-    none.mode = -1;
-    Info cur = decode(info_word(a, p0, false, lane), p0, none, a);
-    Info nxt = decode(info_word(a, p1, same_unit(p1, cur), lane), p1, cur, a);
-    unsigned long long w2 = info_word(a, p2, same_unit(p2, nxt), lane);
-    start_copy(cur, 0);
-    start_copy(nxt, 1);
+    Pos pn;
+    pn.row = gw % a.rows;
+    pn.u = gw / a.rows;
+    pn.chunk = pn.u * a.unit_len;
+    Info q[kNB];
+    {
+        Info prev;
+        prev.mode = -1;
+#pragma unroll
+        for (int i = 0; i < kNB; ++i) {
+            if (i > 0) pn = next_pos(a, pn, nw_row, nw_u);
+            q[i] = decode(info_word(a, pn, same_unit(pn, prev), lane), pn, prev, a);
+            prev = q[i];
+        }
+    }
+    pn = next_pos(a, pn, nw_row, nw_u);
+    unsigned long long wn = info_word(a, pn, same_unit(pn, q[kNB - 1]), lane);
+#pragma unroll
+    for (int i = 0; i < kNB; ++i) start_copy(q[i], i);
     uint32_t en[4];
-    load_entries(cur, en);
+    load_entries(q[0], en);
     int b = 0;
     uint32_t parity = 0u;  // bit bi: parity of buffer bi's next phase
 
@@ -1141,12 +1366,13 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
     bool failed = false;
 
 #pragma unroll 1
-    while (cur.mode != -1) {
-        const Info nn = decode(w2, p2, nxt, a);
-        p2 = next_pos(a, p2, nw_row, nw_u);
-        w2 = info_word(a, p2, same_unit(p2, nn), lane);
+    while (q[0].mode != -1) {
+        const Info nn = decode(wn, pn, q[kNB - 1], a);
+        pn = next_pos(a, pn, nw_row, nw_u);
+        wn = info_word(a, pn, same_unit(pn, nn), lane);
         uint32_t enn[4];
-        load_entries(nxt, enn);
+        load_entries(q[1], enn);
+        const Info& cur = q[0];
         // The row's shared bound (used below), loaded before the copy wait.
         const unsigned long long rb =
             (sel && a.row_th != nullptr && cur.mode == kModeStream) ? __ldcg(a.row_th + cur.row) : 0ull;
@@ -1283,7 +1509,12 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                     const unsigned long long kth = warp_keep_top(L, &n, k, bins);
                     const uint32_t theta = n >= k ? static_cast<uint32_t>(kth >> 32) : 0u;
                     unsigned long long* dst = a.cand + uslot * kUnitCap;
-                    for (int i = lane; i < n; i += 32) dst[i] = L[i];
+                    if (k <= 32) {  // one key a lane, written sorted for the finalize's merge
+                        const unsigned long long key = warp_sort_desc(lane < n ? L[lane] : 0ull, lane);
+                        if (lane < n) dst[lane] = key;
+                    } else {
+                        for (int i = lane; i < n; i += 32) dst[i] = L[i];
+                    }
                     if (lane == 0) {
                         a.cand_n[uslot] = n;
                         a.theta[uslot] = theta;
@@ -1295,6 +1526,23 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
                 }
             }
         }
+        // ---- 7. the row's last unit finalises it (per-row ticket) -------
+        // Each unit's lists are written (or, after a timeout, the row is
+        // marked) before its ticket; the warp taking the row's last ticket
+        // reads every unit's lists and finalises the row. Buffer b is fully
+        // read and not yet refilled: it serves as the finalise's key area.
+        if ((cur.mode == kModeGreedy || cur.mode == kModeStream) && cur.last) {
+            __threadfence();
+            __syncwarp();
+            uint32_t t = 0u;
+            if (lane == 0) t = atomicAdd(a.row_tk + cur.row, 1u);
+            t = __shfl_sync(0xFFFFFFFFu, t, 0);
+            if (t + 1u == static_cast<uint32_t>(a.units)) {
+                __threadfence();
+                finalize_in_stream(a, cur.row, reinterpret_cast<unsigned long long*>(wbase + b * Raw<DT>::kBuf),
+                                   L, bins);
+            }
+        }
         // Every value of the buffer has been read: refill it.
         __syncwarp();
         if (!failed) start_copy(nn, b);
@@ -1302,60 +1550,19 @@ __global__ void __launch_bounds__(kStreamBound, 1) stream_kernel(SampleArgs a, i
         // ---- rotate -------------------------------------------------------
 #pragma unroll
         for (int m = 0; m < 4; ++m) en[m] = enn[m];
-        cur = nxt;
-        nxt = nn;
-        b ^= 1;
+#pragma unroll
+        for (int i = 0; i + 1 < kNB; ++i) q[i] = q[i + 1];
+        q[kNB - 1] = nn;
+        b = b + 1 == kNB ? 0 : b + 1;
     }
     // After a timeout: wait (bounded) for the copies this warp issued, so none
     // lands in shared memory the next CTA on this SM may own.
     if (failed && lane == 0) {
 #pragma unroll
-        for (int bi = 0; bi < 2; ++bi)
+        for (int bi = 0; bi < kNB; ++bi)
             if (issued & (1u << bi)) mbar_wait_bounded(&wbar[warp][bi], (parity >> bi) & 1u, budget);
     }
     __syncwarp();
-}
-
-// Finalises the rows the stream kernel owns, one warp per row, once every unit
-// list of the stream grid is written (launched behind it; griddepcontrol.wait
-// orders its reads after that grid's writes).
-__global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(SampleArgs a) {
-    extern __shared__ __align__(16) unsigned char fdyn[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    unsigned char* wb = fdyn + static_cast<size_t>(warp) * kFinWarpSmem;
-    unsigned long long* L = reinterpret_cast<unsigned long long*>(wb);
-    unsigned long long* S = L + kListCap;
-    unsigned int* bins = reinterpret_cast<unsigned int*>(S + kStreamMaxK);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the general kernel
-    const int row = static_cast<int>(blockIdx.x) * kFinWarps + warp;
-    if (row >= a.rows) return;
-    // Everything the row needs from global memory, issued together.
-    tqfs_params p{};
-    if (!a.top4_only) p = a.params[row];  // no parameters in the top-4 mode
-    long long hs = 0, he = 0, ws, wl;
-    if (a.hist_off != nullptr) {
-        hs = a.hist_off[row];
-        he = a.hist_off[row + 1];
-    }
-    const size_t base = static_cast<size_t>(row) * a.units;
-    const bool lists = !a.top4_only && lane < a.units;
-    const int m_raw = lists ? __ldcg(a.cand_n + base + lane) : 0;
-    const uint32_t th_u = lists ? __ldcg(a.theta + base + lane) : 0u;
-    // The row's per-call word: read, then cleared for the next call.
-    unsigned long long rw = 0ull;
-    if (a.row_th != nullptr) {
-        if (lane == 0) {
-            rw = __ldcg(a.row_th + row);
-            a.row_th[row] = 0ull;
-        }
-        rw = __shfl_sync(0xFFFFFFFFu, rw, 0);
-    }
-    const bool timed_out = (rw & kRowFailed) != 0ull;
-    const int mode = row_mode(p, hs, he, a.hist_off != nullptr, a.vocab_route, a.top4_only != 0, &ws, &wl);
-    if (mode != kModeGreedy && mode != kModeStream) return;
-    finalize_row(a, row, mode == kModeGreedy, static_cast<int>(p.top_k), p, mode == kModeGreedy ? 0 : m_raw,
-                 mode == kModeGreedy ? 0u : th_u, timed_out, L, S, bins);
 }
 
 // Buckets the penalty window of every stream-sampled row by chunk and counts
@@ -1387,20 +1594,14 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
         return;
     }
     for (int i = tid; i <= C; i += NT) cnt[i] = 0u;
-    for (int i = tid; i < kWinWarps * (kChunkLen / 2); i += NT) tbl[i] = 0u;
     __syncthreads();
+    // Tokens are read twice (count, then scatter); the second pass hits L1.
     const int32_t* src = a.hist + ws;
     const int n = static_cast<int>(wl);  // <= kWinCap
-    constexpr int PER = kWinCap / NT;
-    int tok[PER];
-#pragma unroll
-    for (int m = 0; m < PER; ++m) {
-        const int j = tid + m * NT;
-        tok[m] = j < n ? src[j] - a.vocab_offset : -1;  // shard-relative id
+    for (int j = tid; j < n; j += NT) {
+        const int t = src[j] - a.vocab_offset;  // shard-relative id
+        if (t >= 0 && t < a.vocab) atomicAdd(&cnt[t / kChunkLen], 1u);
     }
-#pragma unroll
-    for (int m = 0; m < PER; ++m)
-        if (tok[m] >= 0 && tok[m] < a.vocab) atomicAdd(&cnt[tok[m] / kChunkLen], 1u);
     __syncthreads();
     if (warp == 0) {  // exclusive scan of the C bucket sizes
         const int per = (C + 31) / 32;
@@ -1420,39 +1621,58 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
         if (lane == 31) start[C] = run;
     }
     __syncthreads();
-#pragma unroll
-    for (int m = 0; m < PER; ++m) {
-        const int t = tok[m];
+    for (int j = tid; j < n; j += NT) {
+        const int t = src[j] - a.vocab_offset;
         if (t >= 0 && t < a.vocab) {
             const int c = t / kChunkLen;
             buf[atomicAdd(&cnt[c], 1u)] = static_cast<uint16_t>(t - c * kChunkLen);
         }
     }
     __syncthreads();
-    // Per chunk: count into this warp's 16-bit table, then the lane that
-    // clears an id's count emits (id, count) once, leaving the table clean.
+    // Per chunk, one (id, count) entry per distinct id. A bucket of up to 32
+    // tokens is deduplicated in registers (lanes holding equal ids find each
+    // other with match.any; the lowest emits). Larger buckets count into this
+    // warp's 16-bit table (cleared the first time the warp needs it), and
+    // the lane that clears an id's count emits it, leaving the table clean.
     uint32_t* wt = tbl + warp * (kChunkLen / 2);
     uint32_t* ent = a.win_ent + static_cast<size_t>(row) * kWinCap;
+    bool table_clean = false;
     for (int c = warp; c < C; c += kWinWarps) {
         const uint32_t s0 = start[c], s1 = start[c + 1];
-        if (lane == 0) nd[warp] = 0u;
-        __syncwarp();
-        for (uint32_t i = s0 + lane; i < s1; i += 32) {
-            const uint32_t t = buf[i];
-            atomicAdd(&wt[t >> 1], 1u << (16 * (t & 1u)));
+        uint32_t emitted;
+        if (s1 - s0 <= 32u) {
+            const bool has = s0 + lane < s1;
+            const uint32_t t = has ? buf[s0 + lane] : 0x10000u + lane;  // fillers never match
+            const unsigned grp = __match_any_sync(0xFFFFFFFFu, t);
+            const bool lead = has && lane == __ffs(grp) - 1;
+            const unsigned lb = __ballot_sync(0xFFFFFFFFu, lead);
+            if (lead) ent[s0 + __popc(lb & ((1u << lane) - 1u))] = (t << 16) | static_cast<uint32_t>(__popc(grp));
+            emitted = static_cast<uint32_t>(__popc(lb));
+        } else {
+            if (!table_clean) {
+                for (int i = lane; i < kChunkLen / 2; i += 32) wt[i] = 0u;
+                table_clean = true;
+            }
+            if (lane == 0) nd[warp] = 0u;
+            __syncwarp();
+            for (uint32_t i = s0 + lane; i < s1; i += 32) {
+                const uint32_t t = buf[i];
+                atomicAdd(&wt[t >> 1], 1u << (16 * (t & 1u)));
+            }
+            __syncwarp();
+            for (uint32_t i = s0 + lane; i < s1; i += 32) {
+                const uint32_t t = buf[i];
+                const uint32_t sh = 16 * (t & 1u);
+                const uint32_t old = atomicAnd(&wt[t >> 1], ~(0xFFFFu << sh));
+                const uint32_t count = (old >> sh) & 0xFFFFu;
+                if (count != 0u) ent[s0 + atomicAdd(&nd[warp], 1u)] = (t << 16) | count;
+            }
+            __syncwarp();
+            emitted = nd[warp];
         }
-        __syncwarp();
-        for (uint32_t i = s0 + lane; i < s1; i += 32) {
-            const uint32_t t = buf[i];
-            const uint32_t sh = 16 * (t & 1u);
-            const uint32_t old = atomicAnd(&wt[t >> 1], ~(0xFFFFu << sh));
-            const uint32_t count = (old >> sh) & 0xFFFFu;
-            if (count != 0u) ent[s0 + atomicAdd(&nd[warp], 1u)] = (t << 16) | count;
-        }
-        __syncwarp();
         if (lane == 0) {
             off[2 * c] = s0;
-            off[2 * c + 1] = s0 + nd[warp];
+            off[2 * c + 1] = s0 + emitted;
         }
         __syncwarp();
     }
@@ -1505,19 +1725,19 @@ constexpr size_t kWindowSmem = static_cast<size_t>(2 * (kMaxChunks + 1)) * 4 +
 
 Plan plan_stream(int rows, int vocab, int dtype) {
     Plan pl;
-    (void)dtype;
     pl.chunk_len = kChunkLen;
     pl.chunks = (vocab + pl.chunk_len - 1) / pl.chunk_len;
     if (pl.chunks < 1) pl.chunks = 1;
     if (pl.chunks > kMaxChunks) pl.chunks = 0;
-    pl.smem = static_cast<size_t>(kSW) * kWarpSmem;
+    pl.smem = static_cast<size_t>(dtype == TQFS_DTYPE_F32 ? SL<0>::kSmem : SL<1>::kSmem);
+    const int warps_per_sm = dtype == TQFS_DTYPE_F32 ? SL<0>::kWarps : SL<1>::kWarps;
     // Unit length: a unit costs about its chunks plus kUnitOverhead chunks
     // (its first chunk's full selection and its final list); units run in
     // waves of one per warp. Take the length with the smallest makespan.
     pl.unit_len = (pl.chunks + kMaxUnits - 1) / kMaxUnits;
     pl.units = pl.chunks > 0 ? (pl.chunks + pl.unit_len - 1) / pl.unit_len : 0;
     if (pl.chunks > 0 && rows > 0) {
-        const long long warps = static_cast<long long>(sm_count()) * kSW;
+        const long long warps = static_cast<long long>(sm_count()) * warps_per_sm;
         constexpr int kUnitOverhead = 3;
         long long best = -1;
         const int u_min = (pl.chunks + kMaxUnits - 1) / kMaxUnits;
@@ -1599,7 +1819,7 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     const int top4_diag = a.out_top4 != nullptr && !a.top4_only;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(kST);
+    cfg.blockDim = dim3(static_cast<unsigned>(32 * (a.dtype == TQFS_DTYPE_F32 ? SL<0>::kWarps : SL<1>::kWarps)));
     cfg.dynamicSmemBytes = plan.smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1608,26 +1828,6 @@ cudaError_t launch_stream(const SampleArgs& a_in, const Plan& plan, cudaStream_t
     cfg.attrs = attr;
     cfg.numAttrs = after_window ? 1 : 0;  // overlap its launch with the window kernel
     return cudaLaunchKernelEx(&cfg, kern, a, top4_diag);
-}
-
-cudaError_t launch_finalize(const SampleArgs& a_in, const Plan& plan, cudaStream_t s, bool overlap) {
-    if (a_in.rows <= 0 || plan.units <= 0) return cudaSuccess;
-    const SampleArgs a = with_plan(a_in, plan);
-    const int fin_smem = kFinWarps * kFinWarpSmem;
-    static thread_local unsigned long long done = 0ull;
-    const cudaError_t e = set_smem_once(finalize_kernel, fin_smem, &done);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t fc = {};
-    fc.gridDim = dim3(static_cast<unsigned>((a.rows + kFinWarps - 1) / kFinWarps));
-    fc.blockDim = dim3(kFinWarps * 32);
-    fc.dynamicSmemBytes = static_cast<size_t>(fin_smem);
-    fc.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    fc.attrs = attr;
-    fc.numAttrs = overlap ? 1 : 0;  // launch behind the stream grid
-    return cudaLaunchKernelEx(&fc, finalize_kernel, a);
 }
 
 cudaError_t launch_merge(const MergeArgs& m, cudaStream_t s) {
