@@ -223,13 +223,46 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// An L2 policy that evicts the lines it tags first: the logits are read once,
+// so tagging their copies keeps the kernels' code, parameters, histories and
+// scratch resident in L2 while a batch larger than L2 streams through.
+__device__ __forceinline__ unsigned long long l2_evict_first_policy() {
+    unsigned long long pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// bulk_load with an L2 cache policy (see l2_evict_first_policy).
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes,
+                                               unsigned long long* bar, unsigned long long policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+// try_wait that may suspend the thread until the phase completes or about
+// hint_ns have passed, instead of returning at once: a waiting warp then
+// issues nothing while its copy is in flight.
+__device__ __forceinline__ bool mbar_try_wait_suspend(unsigned long long* bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0u;
+}
 // Wait on an mbarrier phase for at most ~budget_ns: false when it gave up
-// (the caller reports an error instead of spinning forever).
+// (the caller reports an error instead of spinning forever). The clock is
+// read once per suspended try_wait, not on every poll.
 __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity,
                                                   unsigned long long budget_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    const uint32_t hint = budget_ns < 100000ull ? static_cast<uint32_t>(budget_ns) : 100000u;
+    while (!mbar_try_wait_suspend(bar, parity, hint)) {
         if (globaltimer_ns() - t0 > budget_ns) return false;
     }
     return true;

@@ -277,7 +277,7 @@ __device__ __forceinline__ Pos next_pos(const SampleArgs& a, Pos p, int nw_row, 
 // Lanes 0..9 load the row's tqfs_params words and lanes 10..11 its history
 // offsets (skipped within a unit), lanes 12..13 the chunk's window range.
 __device__ __forceinline__ unsigned long long info_word(const SampleArgs& a, Pos p, bool same_unit,
-                                                        int lane) {
+                                                        int lane, bool with_win = true) {
     if (p.u >= a.units) return 0ull;
     if (lane < 12) {
         if (same_unit || a.top4_only) return 0ull;
@@ -285,8 +285,19 @@ __device__ __forceinline__ unsigned long long info_word(const SampleArgs& a, Pos
         if (a.hist_off == nullptr) return 0ull;
         return static_cast<unsigned long long>(__ldg(a.hist_off + p.row + (lane - 10)));
     }
-    if (lane > 13 || a.hist_off == nullptr || a.top4_only) return 0ull;
+    if (!with_win || lane > 13 || a.hist_off == nullptr || a.top4_only) return 0ull;
     return __ldcg(a.win_off + (static_cast<size_t>(p.row) * a.chunks + p.chunk) * 2 + (lane - 12));
+}
+
+// The chunk's window-entry range (written by the window pre-pass), for an
+// Info decoded without it.
+__device__ __forceinline__ void load_window(const SampleArgs& a, Info& f, int lane) {
+    unsigned long long w = 0ull;
+    if (f.mode != -1 && (lane == 12 || lane == 13) && a.hist_off != nullptr && !a.top4_only)
+        w = __ldcg(a.win_off + (static_cast<size_t>(f.row) * a.chunks + f.chunk) * 2 + (lane - 12));
+    f.w0 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 12));
+    f.w1 = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, w, 13));
+    f.pen = f.unit_pen && f.w1 > f.w0;
 }
 
 __device__ __forceinline__ bool same_unit(Pos p, const Info& prev) {
@@ -905,9 +916,13 @@ __device__ __forceinline__ unsigned long long merge_top32(unsigned long long x, 
 // additions, in the same order, as one running sum: each lane keeps its own
 // prefix), so a cut or a draw becomes a ballot over the prefixes.
 __device__ __forceinline__ float seq_prefix(float x, int n, float init, int lane) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __shfl_sync(0xFFFFFFFFu, x, j);
     float c = init, mine = init;
-    for (int j = 0; j < n; ++j) {
-        c = __fadd_rn(c, __shfl_sync(0xFFFFFFFFu, x, j));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j < n) c = __fadd_rn(c, v[j]);
         if (j == lane) mine = c;
     }
     return mine;
@@ -991,28 +1006,32 @@ __device__ __noinline__ int finish_sampled_lanes(const tqfs_params& p, unsigned 
 }
 
 // The row's exact top-k (k <= 32), sorted descending one key a lane, from
-// its units' sorted top-k lists (the union holds the row's top-k): the lists
-// are staged in shared memory in one batch of loads, then merged pairwise.
+// its units' sorted top-k lists (the union holds the row's top-k).
 // *kk gets min(k, keys available).
 __device__ __forceinline__ unsigned long long merge_unit_lists(const SampleArgs& a, int row, int k,
-                                                               unsigned long long* L, int* kk) {
+                                                               int* kk) {
     const int lane = threadIdx.x & 31;
     const int U = a.units;
     const size_t base = static_cast<size_t>(row) * U;
     const int m_own = lane < U ? min(max(__ldcg(a.cand_n + base + lane), 0), k) : 0;
     int avail = warp_sum(m_own);
-    // units beyond the list area (never more than kListCap / 32) are merged as they load
+    // Eight lists at a time are loaded into registers (all loads issued
+    // before any is used), reduced as a tree of independent merges, and
+    // folded into acc. Missing lists and entries are zero keys, which no
+    // merge keeps ahead of a real key.
     unsigned long long acc = 0ull;
-    for (int u0 = 0; u0 < U; u0 += kListCap / 32) {
-        const int nu = min(U - u0, kListCap / 32);
-#pragma unroll 4
-        for (int j = 0; j < nu; ++j) {
-            const int m = __shfl_sync(0xFFFFFFFFu, m_own, u0 + j);
-            L[j * 32 + lane] = lane < m ? __ldcg(a.cand + (base + u0 + j) * kUnitCap + lane) : 0ull;
+    for (int u0 = 0; u0 < U; u0 += 8) {
+        unsigned long long v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int m = __shfl_sync(0xFFFFFFFFu, m_own, (u0 + j) & 31);
+            v[j] = (u0 + j < U && lane < m) ? __ldcg(a.cand + (base + u0 + j) * kUnitCap + lane) : 0ull;
         }
-        __syncwarp();
-        for (int j = 0; j < nu; ++j) acc = merge_top32(acc, L[j * 32 + lane], lane);
-        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = merge_top32(v[2 * j], v[2 * j + 1], lane);
+        v[0] = merge_top32(v[0], v[1], lane);
+        v[2] = merge_top32(v[2], v[3], lane);
+        acc = merge_top32(acc, merge_top32(v[0], v[2], lane), lane);
     }
     *kk = min(avail, k);
     return lane < *kk ? acc : 0ull;
@@ -1075,7 +1094,7 @@ __device__ __forceinline__ void finalize_row(const SampleArgs& a, int row, bool 
     }
     if (!greedy && k <= 32) {
         int kk = 0;
-        const unsigned long long key = merge_unit_lists(a, row, k, L, &kk);
+        const unsigned long long key = merge_unit_lists(a, row, k, &kk);
         if (rec != nullptr) {  // export: the shard's exact top-k, global ids
             if (lane < kk) rec[2 + lane] = key - goff;
             if (lane == 0) {
@@ -1268,9 +1287,6 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
     }
     __syncwarp();
 
-    // Launched right behind the window kernel: wait for its buckets (a no-op
-    // when there is no window kernel in front).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     // The kernel behind this one (general rows, which read only the call's
     // inputs) may launch now; its CTAs find room as this grid's CTAs exit.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1290,6 +1306,7 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
     // stall test hook, a row's copies are armed on the barrier but never
     // issued, so the waits for them run out and nothing is in flight.
     uint32_t issued = 0u;
+    const unsigned long long l2_policy = l2_evict_first_policy();
     auto start_copy = [&](const Info& f, int bi) {
         unsigned char* buf = wbase + bi * Raw<DT>::kBuf;
         const bool copy = f.mode == kModeGreedy || f.mode == kModeStream;
@@ -1307,7 +1324,7 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
         if (lane == 0) {
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&wbar[warp][bi], bulk);
-            if (bulk != 0u && !stall) bulk_load(buf, src, bulk, &wbar[warp][bi]);
+            if (bulk != 0u && !stall) bulk_load_hint(buf, src, bulk, &wbar[warp][bi], l2_policy);
         }
         for (int i = static_cast<int>(bulk) / ES + lane; i < bytes / ES; i += 32) {
             if constexpr (DT == 0)
@@ -1343,14 +1360,20 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
 #pragma unroll
         for (int i = 0; i < kNB; ++i) {
             if (i > 0) pn = next_pos(a, pn, nw_row, nw_u);
-            q[i] = decode(info_word(a, pn, same_unit(pn, prev), lane), pn, prev, a);
+            q[i] = decode(info_word(a, pn, same_unit(pn, prev), lane, false), pn, prev, a);
             prev = q[i];
         }
     }
-    pn = next_pos(a, pn, nw_row, nw_u);
-    unsigned long long wn = info_word(a, pn, same_unit(pn, q[kNB - 1]), lane);
+    // The first copies need only the call's inputs: they are issued before
+    // waiting for the window pre-pass launched in front (its buckets give
+    // the chunks' window ranges; a no-op without a pre-pass).
 #pragma unroll
     for (int i = 0; i < kNB; ++i) start_copy(q[i], i);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < kNB; ++i) load_window(a, q[i], lane);
+    pn = next_pos(a, pn, nw_row, nw_u);
+    unsigned long long wn = info_word(a, pn, same_unit(pn, q[kNB - 1]), lane);
     uint32_t en[4];
     load_entries(q[0], en);
     int b = 0;
@@ -1596,6 +1619,8 @@ __global__ void __launch_bounds__(kWinWarps * 32) window_kernel(SampleArgs a) {
     for (int i = tid; i <= C; i += NT) cnt[i] = 0u;
     __syncthreads();
     // Tokens are read twice (count, then scatter); the second pass hits L1.
+    // (Aggregating the chunk counters' atomics per warp with match.any was
+    // measured slower: 2.3 against 0.5 us for this loop on c1x256.)
     const int32_t* src = a.hist + ws;
     const int n = static_cast<int>(wl);  // <= kWinCap
     for (int j = tid; j < n; j += NT) {
