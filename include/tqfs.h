@@ -263,10 +263,23 @@ int tqfs_shard_merge(tqfs_handle* handle, const uint64_t* recs_dev, int nranks, 
                      int32_t* out_status_dev, void* stream);
 /* NCCL (libnccl.so.2, loaded at run time): a 128-byte unique id made on one
  * rank and shared by the caller, one communicator per rank on the handle's
- * device. */
+ * device. Communicators are non-blocking where the NCCL has them (2.14+):
+ * tqfs_nccl_comm_init_timeout waits at most timeout_ms for every rank to
+ * join, then aborts the communicator and returns TQFS_ERR_TIMEOUT (a rank
+ * that never joins cannot hang the others); tqfs_nccl_comm_init is the same
+ * with a 120 s deadline. The reference's GPU waits are bounded the same way
+ * (EventFence::wait_until_signaled, src/backend/metal/timing.rs:68-79). */
 int tqfs_nccl_unique_id(void* id_out);
 int tqfs_nccl_comm_init(tqfs_handle* handle, int nranks, int rank, const void* id, void** comm_out);
+int tqfs_nccl_comm_init_timeout(tqfs_handle* handle, int nranks, int rank, const void* id,
+                                int timeout_ms, void** comm_out);
 int tqfs_nccl_comm_destroy(void* comm);
+/* Host watchdog over the collectives issued on `stream`: returns TQFS_OK once
+ * the stream's work is done and the communicator reports no error; after
+ * timeout_ms, or on an NCCL error, aborts the communicator (ending its
+ * kernels that still wait on a peer) and returns TQFS_ERR_TIMEOUT or
+ * TQFS_ERR_NCCL. Synchronising. */
+int tqfs_nccl_wait(tqfs_handle* handle, void* comm, void* stream, int timeout_ms);
 /* Export, ncclAllGather over the communicator, merge: one call per rank, on
  * `stream`. */
 int tqfs_sample_vocab_sharded(tqfs_handle* handle, void* comm, int nranks, const void* logits_dev,

@@ -78,3 +78,25 @@ def test_stall_hook_rejects_bad_arguments(cuda_device):
     h = N.default_handle(0)
     assert N.lib().tqfs_debug_stall_row(h.ptr, -1, WAIT_NS) == N.ERR_INVALID_ARG
     assert N.lib().tqfs_debug_stall_row(h.ptr, 0, 0) == N.ERR_INVALID_ARG
+
+
+def test_nccl_rank_that_never_joins_times_out(cuda_device):
+    """Host-side failure: a 2-rank communicator whose second rank never joins.
+    Rank 0's init must give up within its deadline with TQFS_ERR_TIMEOUT
+    (the communicator is aborted) instead of hanging."""
+    import ctypes
+    import time
+    h = N.Handle(0)
+    uid = (ctypes.c_uint8 * 128)()
+    st = N.lib().tqfs_nccl_unique_id(ctypes.addressof(uid))
+    if st != N.OK:
+        pytest.skip("NCCL not available")
+    comm = ctypes.c_void_p()
+    t0 = time.monotonic()
+    st = N.lib().tqfs_nccl_comm_init_timeout(h.ptr, 2, 0, ctypes.addressof(uid), 2000, ctypes.byref(comm))
+    dt = time.monotonic() - t0
+    assert st == N.ERR_TIMEOUT, (st, N.lib().tqfs_last_error(h.ptr))
+    assert not comm.value
+    assert dt < 30.0, dt
+    assert b"aborted" in N.lib().tqfs_last_error(h.ptr)
+    h.close()

@@ -39,7 +39,8 @@ EXPORTS = [
     "tqfs_set_timing", "tqfs_get_timing", "tqfs_stream_plan", "tqfs_debug_stall_row", "tqfs_xoshiro_from_seed", "tqfs_xoshiro_next_u64",
     "tqfs_xoshiro_next_f32", "tqfs_sample", "tqfs_sample_host", "tqfs_top_logit_candidates",
     "tqfs_apply_penalties", "tqfs_mtp_verify", "tqfs_shard_record_words", "tqfs_shard_export",
-    "tqfs_shard_merge", "tqfs_nccl_unique_id", "tqfs_nccl_comm_init", "tqfs_nccl_comm_destroy",
+    "tqfs_shard_merge", "tqfs_nccl_unique_id", "tqfs_nccl_comm_init", "tqfs_nccl_comm_init_timeout", "tqfs_nccl_comm_destroy",
+    "tqfs_nccl_wait",
     "tqfs_sample_vocab_sharded", "tqfs_sample_static", "tqfs_sampler_new", "tqfs_sampler_is_greedy", "tqfs_sampler_select", "tqfs_sampler_get_state",
     "tqfs_sampler_free",
 ]
@@ -115,6 +116,8 @@ def lib() -> ctypes.CDLL:
     L.tqfs_nccl_unique_id.argtypes = [vp]
     L.tqfs_nccl_comm_init.argtypes = [vp, i32, i32, vp, ctypes.POINTER(vp)]
     L.tqfs_nccl_comm_destroy.argtypes = [vp]
+    L.tqfs_nccl_comm_init_timeout.argtypes = [vp, i32, i32, vp, i32, ctypes.POINTER(vp)]
+    L.tqfs_nccl_wait.argtypes = [vp, vp, vp, i32]
     L.tqfs_sample_vocab_sharded.argtypes = [vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, vp, vp, vp, vp, vp,
                                             vp, vp, vp]
     L.tqfs_sampler_new.argtypes = [vp, ctypes.POINTER(Params), i32, u64, ctypes.POINTER(vp)]

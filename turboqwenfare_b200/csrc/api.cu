@@ -10,6 +10,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -674,7 +675,29 @@ typedef struct {
     char internal[128];
 } NcclUniqueId;
 using NcclComm = void*;
-enum { kNcclSuccess = 0, kNcclUint64 = 5 };
+enum { kNcclSuccess = 0, kNcclUint64 = 5, kNcclInProgress = 7 };
+// ncclConfig_t as NCCL 2.27 lays it out (nccl.h, NCCL_CONFIG_INITIALIZER):
+// NCCL reads a caller's config by its size and version fields, so later
+// NCCL releases accept this layout too. Only `blocking` is set; every other
+// field keeps NCCL's "undefined" marker (INT_MIN, or a null pointer).
+struct NcclConfig {
+    size_t size = sizeof(NcclConfig);
+    unsigned int magic = 0xcafebeefu;
+    unsigned int version = 22700u;
+    int blocking = kUndefInt;
+    int cga_cluster_size = kUndefInt;
+    int min_ctas = kUndefInt;
+    int max_ctas = kUndefInt;
+    const char* net_name = nullptr;
+    int split_share = kUndefInt;
+    int traffic_class = kUndefInt;
+    const char* comm_name = nullptr;
+    int collnet_enable = kUndefInt;
+    int cta_policy = kUndefInt;
+    int shrink_share = kUndefInt;
+    int nvls_ctas = kUndefInt;
+    static constexpr int kUndefInt = static_cast<int>(0x80000000u);
+};
 struct NcclApi {
     bool tried = false;
     void* dl = nullptr;
@@ -683,6 +706,10 @@ struct NcclApi {
     int (*all_gather)(const void*, void*, size_t, int, NcclComm, cudaStream_t) = nullptr;
     int (*comm_destroy)(NcclComm) = nullptr;
     const char* (*error_string)(int) = nullptr;
+    // optional (NCCL >= 2.14): non-blocking communicators and their abort
+    int (*comm_init_rank_config)(NcclComm*, int, NcclUniqueId, int, NcclConfig*) = nullptr;
+    int (*comm_get_async_error)(NcclComm, int*) = nullptr;
+    int (*comm_abort)(NcclComm) = nullptr;
 };
 std::mutex g_nccl_mutex;
 NcclApi g_nccl;
@@ -700,6 +727,10 @@ const NcclApi* nccl() {
                 dlsym(dl, "ncclAllGather"));
             g_nccl.comm_destroy = reinterpret_cast<int (*)(NcclComm)>(dlsym(dl, "ncclCommDestroy"));
             g_nccl.error_string = reinterpret_cast<const char* (*)(int)>(dlsym(dl, "ncclGetErrorString"));
+            g_nccl.comm_init_rank_config = reinterpret_cast<int (*)(NcclComm*, int, NcclUniqueId, int, NcclConfig*)>(
+                dlsym(dl, "ncclCommInitRankConfig"));
+            g_nccl.comm_get_async_error = reinterpret_cast<int (*)(NcclComm, int*)>(dlsym(dl, "ncclCommGetAsyncError"));
+            g_nccl.comm_abort = reinterpret_cast<int (*)(NcclComm)>(dlsym(dl, "ncclCommAbort"));
             if (g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_gather && g_nccl.comm_destroy &&
                 g_nccl.error_string)
                 g_nccl.dl = dl;
@@ -711,6 +742,49 @@ const NcclApi* nccl() {
 int nccl_fail(tqfs_handle* h, const NcclApi* n, int r, const char* what) {
     return fail(h, TQFS_ERR_NCCL, "%s: %s", what, n->error_string(r));
 }
+
+bool nccl_nonblocking(const NcclApi* n) {
+    return n->comm_init_rank_config && n->comm_get_async_error && n->comm_abort;
+}
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Polls a non-blocking communicator (and, with a stream, that stream's work)
+// until both are done or timeout_ms passes. On expiry or on an NCCL error
+// the communicator is aborted, which also ends its kernels still waiting on
+// a peer; the caller must not use it again.
+int nccl_poll(tqfs_handle* h, const NcclApi* n, NcclComm c, cudaStream_t s, bool with_stream, double timeout_ms,
+              const char* what) {
+    const double t0 = now_ms();
+    for (;;) {
+        int state = kNcclSuccess;
+        const int r = n->comm_get_async_error(c, &state);
+        if (r != kNcclSuccess || (state != kNcclSuccess && state != kNcclInProgress)) {
+            n->comm_abort(c);
+            return nccl_fail(h, n, r != kNcclSuccess ? r : state, what);
+        }
+        bool stream_done = true;
+        if (with_stream) {
+            const cudaError_t q = cudaStreamQuery(s);
+            if (q != cudaSuccess && q != cudaErrorNotReady) {
+                n->comm_abort(c);
+                return cuda_fail(h, q, what);
+            }
+            stream_done = q == cudaSuccess;
+        }
+        if (state == kNcclSuccess && stream_done) return TQFS_OK;
+        if (now_ms() - t0 > timeout_ms) {
+            n->comm_abort(c);
+            return fail(h, TQFS_ERR_TIMEOUT, "%s: no completion within %.0f ms; communicator aborted", what,
+                        timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+constexpr double kDefaultNcclInitMs = 120000.0;
 
 }  // namespace
 
@@ -724,8 +798,10 @@ int tqfs_nccl_unique_id(void* id_out) {
     return TQFS_OK;
 }
 
-int tqfs_nccl_comm_init(tqfs_handle* h, int nranks, int rank, const void* id, void** comm_out) {
-    if (!h || !id || !comm_out || nranks <= 0 || rank < 0 || rank >= nranks) return TQFS_ERR_INVALID_ARG;
+int tqfs_nccl_comm_init_timeout(tqfs_handle* h, int nranks, int rank, const void* id, int timeout_ms,
+                                void** comm_out) {
+    if (!h || !id || !comm_out || nranks <= 0 || rank < 0 || rank >= nranks || timeout_ms <= 0)
+        return TQFS_ERR_INVALID_ARG;
     *comm_out = nullptr;
     const NcclApi* n = nccl();
     if (n == nullptr) return fail(h, TQFS_ERR_NCCL, "libnccl.so.2 not found");
@@ -734,10 +810,41 @@ int tqfs_nccl_comm_init(tqfs_handle* h, int nranks, int rank, const void* id, vo
     NcclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     NcclComm c = nullptr;
-    const int r = n->comm_init_rank(&c, nranks, uid, rank);
-    if (r != kNcclSuccess) return nccl_fail(h, n, r, "ncclCommInitRank");
+    if (!nccl_nonblocking(n)) {  // an NCCL without non-blocking communicators: no deadline
+        const int r = n->comm_init_rank(&c, nranks, uid, rank);
+        if (r != kNcclSuccess) return nccl_fail(h, n, r, "ncclCommInitRank");
+        *comm_out = c;
+        return TQFS_OK;
+    }
+    NcclConfig cfg;
+    cfg.blocking = 0;
+    const int r = n->comm_init_rank_config(&c, nranks, uid, rank, &cfg);
+    if (r != kNcclSuccess && r != kNcclInProgress) {
+        if (c != nullptr) n->comm_abort(c);
+        return nccl_fail(h, n, r, "ncclCommInitRankConfig");
+    }
+    st = nccl_poll(h, n, c, nullptr, false, static_cast<double>(timeout_ms), "ncclCommInitRankConfig");
+    if (st != TQFS_OK) return st;
     *comm_out = c;
     return TQFS_OK;
+}
+
+int tqfs_nccl_comm_init(tqfs_handle* h, int nranks, int rank, const void* id, void** comm_out) {
+    return tqfs_nccl_comm_init_timeout(h, nranks, rank, id, static_cast<int>(kDefaultNcclInitMs), comm_out);
+}
+
+int tqfs_nccl_wait(tqfs_handle* h, void* comm, void* stream, int timeout_ms) {
+    if (!h || !comm || timeout_ms <= 0) return TQFS_ERR_INVALID_ARG;
+    const NcclApi* n = nccl();
+    if (n == nullptr) return fail(h, TQFS_ERR_NCCL, "libnccl.so.2 not found");
+    int st = ensure_current(h);
+    if (st != TQFS_OK) return st;
+    if (!nccl_nonblocking(n)) {
+        const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? TQFS_OK : cuda_fail(h, e, "stream");
+    }
+    return nccl_poll(h, n, comm, static_cast<cudaStream_t>(stream), true, static_cast<double>(timeout_ms),
+                     "collective");
 }
 
 int tqfs_nccl_comm_destroy(void* comm) {
@@ -768,7 +875,13 @@ int tqfs_sample_vocab_sharded(tqfs_handle* h, void* comm, int nranks, const void
                            hist_off_dev, params_dev, send, stream);
     if (st != TQFS_OK) return st;
     const int r = n->all_gather(send, recv, words, kNcclUint64, comm, static_cast<cudaStream_t>(stream));
-    if (r != kNcclSuccess) return nccl_fail(h, n, r, "ncclAllGather");
+    if (r == kNcclInProgress && nccl_nonblocking(n)) {
+        // a non-blocking communicator enqueues in the background: wait (bounded) for the enqueue only
+        st = nccl_poll(h, n, comm, nullptr, false, kDefaultNcclInitMs, "ncclAllGather");
+        if (st != TQFS_OK) return st;
+    } else if (r != kNcclSuccess) {
+        return nccl_fail(h, n, r, "ncclAllGather");
+    }
     return tqfs_shard_merge(h, recv, nranks, rows, vocab_total, hist_off_dev, params_dev, uniforms_dev,
                             rng_state_dev, out_token_dev, out_status_dev, stream);
 }

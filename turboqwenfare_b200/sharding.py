@@ -84,7 +84,8 @@ class NcclComm:
     """A library-owned NCCL communicator over the ranks of a torch.distributed
     group; the unique id travels over that group (any backend)."""
 
-    def __init__(self, rank: int, nranks: int, device: int, group=None, handle: Optional[N.Handle] = None):
+    def __init__(self, rank: int, nranks: int, device: int, group=None, handle: Optional[N.Handle] = None,
+                 timeout_ms: int = 120_000):
         import ctypes
         import torch
         import torch.distributed as dist
@@ -105,10 +106,18 @@ class NcclComm:
             dist.broadcast(uid, 0, group=group)
         idbuf = (ctypes.c_uint8 * 128)(*uid.tolist())
         comm = ctypes.c_void_p()
-        self.handle.check(N.lib().tqfs_nccl_comm_init(self.handle.ptr, nranks, rank, ctypes.addressof(idbuf),
-                                                      ctypes.byref(comm)))
+        self.handle.check(N.lib().tqfs_nccl_comm_init_timeout(self.handle.ptr, nranks, rank, ctypes.addressof(idbuf),
+                                                              int(timeout_ms), ctypes.byref(comm)))
         self.ptr = comm.value
         self.rank, self.nranks = rank, nranks
+
+    def wait(self, stream=None, timeout_ms: int = 10_000) -> None:
+        """Host watchdog over this communicator's collectives on `stream` (the
+        current stream by default): raises TqfsError (TIMEOUT) and aborts the
+        communicator when they do not complete within timeout_ms."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        self.handle.check(N.lib().tqfs_nccl_wait(self.handle.ptr, self.ptr, s.cuda_stream, int(timeout_ms)))
 
     def close(self) -> None:
         if self.ptr:
