@@ -87,7 +87,22 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
         const tqfs_params p = a.params[row];
         const size_t base = static_cast<size_t>(row) * a.ld;
         // ---- penalised candidates in token order (mod.rs:90-99, 114-148) --
-        for (int i = tid; i < V; i += kGenThreads) W[i] = logit_at<DT>(a.logits, base, i);
+        // Loads go out in batches before any store: W and the logits could
+        // alias as far as the compiler knows, so a load after a store would
+        // wait for it and every iteration would pay a full memory latency.
+        for (int i0 = 0; i0 < V; i0 += kGenThreads * kBatch) {
+            float v[kBatch];
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q) {
+                const int i = i0 + q * kGenThreads + tid;
+                v[q] = i < V ? logit_at<DT>(a.logits, base, i) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q) {
+                const int i = i0 + q * kGenThreads + tid;
+                if (i < V) W[i] = v[q];
+            }
+        }
         const bool pen = !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f &&
                            p.presence_penalty == 0.0f);
         long long wstart = 0, wlen = 0;
@@ -98,19 +113,38 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
             wstart = he - wlen;
         }
         __syncthreads();
-        if (wlen > 0) {
-            for (long long j = tid; j < wlen; j += kGenThreads) {
-                const int t = a.hist[wstart + j];
-                if (t >= 0 && t < V) atomicAdd(C + t, 1u);
+        if (wlen > 0) {  // history loads batched ahead of the atomics, as above
+            for (long long j0 = 0; j0 < wlen; j0 += kGenThreads * kBatch) {
+                int t[kBatch];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    const long long j = j0 + q * kGenThreads + tid;
+                    t[q] = j < wlen ? a.hist[wstart + j] : -1;
+                }
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q)
+                    if (t[q] >= 0 && t[q] < V) atomicAdd(C + t[q], 1u);
             }
             __syncthreads();
-            for (long long j = tid; j < wlen; j += kGenThreads) {
-                const int t = a.hist[wstart + j];
-                if (t >= 0 && t < V) {
-                    const unsigned int c = atomicExch(C + t, 0u);  // leaves C zero
-                    if (c != 0u)
-                        W[t] = penalise(logit_at<DT>(a.logits, base, t), c, p.repeat_penalty,
-                                        p.frequency_penalty, p.presence_penalty);
+            for (long long j0 = 0; j0 < wlen; j0 += kGenThreads * kBatch) {
+                int t[kBatch];
+                float lv[kBatch];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    const long long j = j0 + q * kGenThreads + tid;
+                    t[q] = j < wlen ? a.hist[wstart + j] : -1;
+                }
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q)
+                    lv[q] = (t[q] >= 0 && t[q] < V) ? logit_at<DT>(a.logits, base, t[q]) : 0.0f;
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    if (t[q] >= 0 && t[q] < V) {
+                        const unsigned int c = atomicExch(C + t[q], 0u);  // leaves C zero
+                        if (c != 0u)
+                            W[t[q]] = penalise(lv[q], c, p.repeat_penalty, p.frequency_penalty,
+                                               p.presence_penalty);
+                    }
                 }
             }
             __syncthreads();

@@ -53,9 +53,24 @@ __device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta) {
     return w;
 }
 
+// The row's logits into W, loads batched ahead of the stores (the compiler
+// cannot tell that W and the logits do not alias, so an unbatched loop pays
+// a full memory latency per element).
 template <int DT>
 __device__ void load_row(const MtpArgs& m, const void* base, size_t row, float* W) {
-    for (int i = threadIdx.x; i < m.vocab; i += kMT) W[i] = logit_at<DT>(base, row * m.ld, i);
+    for (int i0 = 0; i0 < m.vocab; i0 += kMT * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int i = i0 + q * kMT + threadIdx.x;
+            v[q] = i < m.vocab ? logit_at<DT>(base, row * m.ld, i) : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int i = i0 + q * kMT + threadIdx.x;
+            if (i < m.vocab) W[i] = v[q];
+        }
+    }
     __syncthreads();
 }
 
