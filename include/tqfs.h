@@ -318,6 +318,30 @@ int tqfs_sample_static(const void* logits_dev, int dtype, int rows, int vocab, i
                        uint64_t* rng_state_dev, int32_t* out_token_dev,
                        int32_t* out_status_dev, void* stream);
 
+/* ---- batched decode loop bookkeeping (device) ---------------------------- */
+/*
+ * The per-request loop of src/runtime/generation.rs:714-770 for a batch of
+ * rows, on the device: `generated` (the penalty history) gets each row's
+ * token, and a row stops at its end-of-sequence token (eos_dev; -1: none) or
+ * after max_tokens_dev pushes. History layout, in the packed form
+ * tqfs_sample reads: row r owns hist_dev[r*cap, (r+1)*cap), its len_dev[r]
+ * tokens from the slot's start, hist_off_dev[r+1] = r*cap + len[r],
+ * hist_off_dev[0] = 0. A row's range in that form starts with the previous
+ * slot's unused tail, which holds -1; ids outside [0, vocab) never match
+ * (src/sampling/mod.rs:135-138), so the penalties equal the reference's.
+ * No counterpart in the reference (its loop runs one request on the host).
+ *   tqfs_decode_begin: generated = [first token]; done where that token is
+ *     the eos or max_tokens <= 1.
+ *   tqfs_decode_append: rows not done push tokens_dev[r] and may stop; done
+ *     rows are left as they are (their sampled token is ignored).
+ */
+int tqfs_decode_begin(int rows, int cap, const int32_t* first_tokens_dev, int32_t* hist_dev,
+                      int64_t* hist_off_dev, int32_t* len_dev, const int32_t* eos_dev,
+                      const int32_t* max_tokens_dev, uint8_t* done_dev, void* stream);
+int tqfs_decode_append(int rows, int cap, const int32_t* tokens_dev, int32_t* hist_dev,
+                       int64_t* hist_off_dev, int32_t* len_dev, const int32_t* eos_dev,
+                       const int32_t* max_tokens_dev, uint8_t* done_dev, void* stream);
+
 /* ---- drop-in Sampler (host pointers; synchronising) ---------------------- */
 /*
  * `Sampler::new(&SamplingParams)` (src/sampling/mod.rs:45-53): greedy iff
