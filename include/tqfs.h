@@ -333,7 +333,16 @@ int tqfs_sample_static(const void* logits_dev, int dtype, int rows, int vocab, i
  *   tqfs_decode_begin: generated = [first token]; done where that token is
  *     the eos or max_tokens <= 1.
  *   tqfs_decode_append: rows not done push tokens_dev[r] and may stop; done
- *     rows are left as they are (their sampled token is ignored).
+ *     rows are left as they are (their sampled token is ignored). A negative
+ *     token (a failed row) stops the row with done = 2 and pushes nothing.
+ *   tqfs_mtp_commit: commits one tqfs_mtp_verify per row: rows not done push
+ *     their accepted drafts (drafts_dev[r*L .. r*L + accepted)) and then
+ *     tokens_dev[r], each under the stop rules of one append; emitted_dev
+ *     (optional) gets the tokens pushed. Extends the single-pair outcome of
+ *     verify_pair (src/runtime/mtp.rs:92-104: 2 tokens on accept, 1 on reject)
+ *     to L drafts. A model's KV cache then keeps len - 1 entries per row (the
+ *     newest token is the next step's input); the entries of rejected drafts
+ *     are the ones it discards.
  */
 int tqfs_decode_begin(int rows, int cap, const int32_t* first_tokens_dev, int32_t* hist_dev,
                       int64_t* hist_off_dev, int32_t* len_dev, const int32_t* eos_dev,
@@ -341,6 +350,19 @@ int tqfs_decode_begin(int rows, int cap, const int32_t* first_tokens_dev, int32_
 int tqfs_decode_append(int rows, int cap, const int32_t* tokens_dev, int32_t* hist_dev,
                        int64_t* hist_off_dev, int32_t* len_dev, const int32_t* eos_dev,
                        const int32_t* max_tokens_dev, uint8_t* done_dev, void* stream);
+int tqfs_mtp_commit(int rows, int draft_len, int cap, const int32_t* accepted_dev,
+                    const int32_t* tokens_dev, const int32_t* drafts_dev, int32_t* hist_dev,
+                    int64_t* hist_off_dev, int32_t* len_dev, const int32_t* eos_dev,
+                    const int32_t* max_tokens_dev, uint8_t* done_dev, int32_t* emitted_dev,
+                    void* stream);
+/*
+ * Draws `count` uniforms per row from each row's xoshiro256++ state
+ * (rng_state_dev: rows x 4 u64, advanced in place) as
+ * Xoshiro256PlusPlus::next_f32 does (src/sampling/mod.rs:311-331):
+ * (next_u64 >> 40) / 2^24. out_dev: rows x count floats. Gives a device loop
+ * the MTP verify uniforms from each request's own generator.
+ */
+int tqfs_rng_draw(int rows, int count, uint64_t* rng_state_dev, float* out_dev, void* stream);
 
 /* ---- drop-in Sampler (host pointers; synchronising) ---------------------- */
 /*

@@ -44,3 +44,18 @@ def test_oracle_verify_pair_agrees():
     import oracle as O
     assert O.verify_pair(42, 42) == 2
     assert O.verify_pair(42, 7) == 1
+
+
+def test_net_benefit_entry_is_record_and_decide_shifted_by_one():
+    a, b = MtpController(3), MtpController(3)
+    for e in [2, 2, 1, 0, 0, 0, 2, 2, 2, 2]:
+        assert a.record_and_decide(e) == b.record_net_benefit(e - 1.0)
+        assert a.window == b.window and a.window_full() == b.window_full()
+
+
+def test_time_charged_net_benefit_keeps_mtp_off():
+    """A verification that emits 2 tokens in 2.5 plain steps' time is a loss."""
+    c = MtpController(4)
+    for _ in range(8):
+        c.record_net_benefit(2.0 - 2.5)
+    assert not c.enabled()

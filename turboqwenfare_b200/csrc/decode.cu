@@ -13,11 +13,21 @@
 // last min(repeat_last_n, range) entries, therefore counts exactly the
 // tokens of the reference's window (the last min(repeat_last_n, len)
 // tokens), and an append is one store and one offset update.
+//
+// A row whose sampled token is negative (the sampler's failure token) stops
+// with done = 2 and pushes nothing.
+//
+// An MTP step (src/runtime/mtp.rs:92-104, batched by tqfs_mtp_verify)
+// commits a variable number of tokens per row: the accepted drafts, then the
+// verify token, each pushed under the same stop rules as one append. The
+// generator draws for the verify's uniforms come from the rows' own
+// xoshiro256++ states, so a loop's randomness stays one stream per request.
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "../../include/tqfs.h"
+#include "common.cuh"
 
 namespace {
 
@@ -45,6 +55,10 @@ __global__ void decode_append_kernel(int rows, int cap, const int32_t* tokens, i
     if (r >= rows || done[r]) return;
     const int n = len[r];
     const int t = tokens[r];
+    if (t < 0) {  // the sampler failed this row
+        done[r] = 2;
+        return;
+    }
     if (n >= cap) {  // no room: the row stops (cap bounds the tokens a row may generate)
         done[r] = 1;
         return;
@@ -53,6 +67,51 @@ __global__ void decode_append_kernel(int rows, int cap, const int32_t* tokens, i
     len[r] = n + 1;
     hist_off[r + 1] = static_cast<long long>(r) * cap + n + 1;
     if (t == eos[r] || n + 1 >= max_tokens[r]) done[r] = 1;
+}
+
+__global__ void mtp_commit_kernel(int rows, int L, int cap, const int32_t* accepted, const int32_t* tokens,
+                                  const int32_t* drafts, int32_t* hist, int64_t* hist_off, int32_t* len,
+                                  const int32_t* eos, const int32_t* max_tokens, uint8_t* done, int32_t* emitted) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    if (done[r]) {
+        if (emitted) emitted[r] = 0;
+        return;
+    }
+    const int t_last = tokens[r];
+    int a = accepted[r];
+    a = a < 0 ? 0 : (a > L ? L : a);
+    int n = len[r];
+    const int n0 = n;
+    uint8_t d = 0;
+    if (t_last < 0) {
+        d = 2;
+    } else {
+        const int e = eos[r], mx = max_tokens[r];
+        int32_t* h = hist + static_cast<long long>(r) * cap;
+        for (int i = 0; i <= a && !d; ++i) {
+            const int t = i < a ? drafts[static_cast<long long>(r) * L + i] : t_last;
+            if (n >= cap) {
+                d = 1;
+                break;
+            }
+            h[n++] = t;
+            if (t == e || n >= mx) d = 1;
+        }
+    }
+    len[r] = n;
+    hist_off[r + 1] = static_cast<long long>(r) * cap + n;
+    done[r] = d;
+    if (emitted) emitted[r] = n - n0;
+}
+
+__global__ void rng_draw_kernel(int rows, int count, uint64_t* state, float* out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    uint64_t s[4];
+    for (int q = 0; q < 4; ++q) s[q] = state[static_cast<size_t>(r) * 4 + q];
+    for (int i = 0; i < count; ++i) out[static_cast<size_t>(r) * count + i] = tqfs::xoshiro_next_f32(s);
+    for (int q = 0; q < 4; ++q) state[static_cast<size_t>(r) * 4 + q] = s[q];
 }
 
 }  // namespace
@@ -82,6 +141,30 @@ int tqfs_decode_append(int rows, int cap, const int32_t* tokens_dev, int32_t* hi
         return TQFS_ERR_INVALID_ARG;
     decode_append_kernel<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
         rows, cap, tokens_dev, hist_dev, hist_off_dev, len_dev, eos_dev, max_tokens_dev, done_dev);
+    return cudaGetLastError() == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
+}
+
+int tqfs_mtp_commit(int rows, int draft_len, int cap, const int32_t* accepted_dev, const int32_t* tokens_dev,
+                    const int32_t* drafts_dev, int32_t* hist_dev, int64_t* hist_off_dev, int32_t* len_dev,
+                    const int32_t* eos_dev, const int32_t* max_tokens_dev, uint8_t* done_dev,
+                    int32_t* emitted_dev, void* stream) {
+    if (rows < 0 || cap < 1 || draft_len < 0) return TQFS_ERR_INVALID_ARG;
+    if (rows == 0) return TQFS_OK;
+    if (!accepted_dev || !tokens_dev || (draft_len > 0 && !drafts_dev) || !hist_dev || !hist_off_dev ||
+        !len_dev || !eos_dev || !max_tokens_dev || !done_dev)
+        return TQFS_ERR_INVALID_ARG;
+    mtp_commit_kernel<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        rows, draft_len, cap, accepted_dev, tokens_dev, drafts_dev, hist_dev, hist_off_dev, len_dev, eos_dev,
+        max_tokens_dev, done_dev, emitted_dev);
+    return cudaGetLastError() == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
+}
+
+int tqfs_rng_draw(int rows, int count, uint64_t* rng_state_dev, float* out_dev, void* stream) {
+    if (rows < 0 || count < 0) return TQFS_ERR_INVALID_ARG;
+    if (rows == 0 || count == 0) return TQFS_OK;
+    if (!rng_state_dev || !out_dev) return TQFS_ERR_INVALID_ARG;
+    rng_draw_kernel<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(rows, count, rng_state_dev,
+                                                                                         out_dev);
     return cudaGetLastError() == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
 }
 

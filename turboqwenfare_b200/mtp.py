@@ -74,8 +74,17 @@ class MtpController:
     def _rolling_net_benefit(self) -> float:
         return 0.0 if not self.window else sum(self.window) / len(self.window)
 
+    def window_full(self) -> bool:
+        return len(self.window) == self.window_capacity
+
     def record_and_decide(self, emitted_tokens: int) -> bool:
-        net_benefit = float(emitted_tokens) - 1.0
+        return self.record_net_benefit(float(emitted_tokens) - 1.0)
+
+    def record_net_benefit(self, net_benefit: float) -> bool:
+        """The body of record_and_decide (mtp.rs:147-168) for a net benefit
+        the caller has already computed; record_and_decide(e) is
+        record_net_benefit(e - 1.0). A loop that charges a speculative step's
+        extra time against it passes emitted - t_speculative / t_plain."""
         if len(self.window) == self.window_capacity:
             self.window.pop(0)
         self.window.append(net_benefit)
