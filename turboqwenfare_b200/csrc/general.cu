@@ -30,6 +30,15 @@ namespace tqfs {
 namespace {
 
 constexpr int kGenThreads = kFilterThreads;
+// Penalty windows up to kPenHashMax tokens count in a shared-memory hash
+// table (kPenHashSlots keys and counts in the sort buffer); longer windows
+// count in the global counts array.
+constexpr int kPenHashBits = 14;
+constexpr int kPenHashSlots = 1 << kPenHashBits;
+constexpr int kPenHashMax = kPenHashSlots * 3 / 4;
+constexpr unsigned kPenEmpty = 0xFFFFFFFFu;
+static_assert(kPenHashSlots * 8 <= kSegCap * 8, "the table fits the sort buffer");
+static_assert(kPenHashSlots % (kFilterThreads * kBatch) == 0, "table pass");
 
 // Rows the stream path does not own (row_mode in common.cuh).
 __device__ __forceinline__ bool is_general(const SampleArgs& a, int row, const tqfs_params& p) {
@@ -90,19 +99,7 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
         // Loads go out in batches before any store: W and the logits could
         // alias as far as the compiler knows, so a load after a store would
         // wait for it and every iteration would pay a full memory latency.
-        for (int i0 = 0; i0 < V; i0 += kGenThreads * kBatch) {
-            float v[kBatch];
-#pragma unroll
-            for (int q = 0; q < kBatch; ++q) {
-                const int i = i0 + q * kGenThreads + tid;
-                v[q] = i < V ? logit_at<DT>(a.logits, base, i) : 0.0f;
-            }
-#pragma unroll
-            for (int q = 0; q < kBatch; ++q) {
-                const int i = i0 + q * kGenThreads + tid;
-                if (i < V) W[i] = v[q];
-            }
-        }
+        load_row_to<DT, kGenThreads>(a.logits, base, V, W);
         const bool pen = !(p.repeat_penalty == 1.0f && p.frequency_penalty == 0.0f &&
                            p.presence_penalty == 0.0f);
         long long wstart = 0, wlen = 0;
@@ -113,7 +110,54 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
             wstart = he - wlen;
         }
         __syncthreads();
-        if (wlen > 0) {  // history loads batched ahead of the atomics, as above
+        if (wlen > 0 && wlen <= kPenHashMax) {
+            // The window's counts in a hash table in shared memory (open
+            // addressing on the token), then one pass over the table.
+            unsigned int* hk = reinterpret_cast<unsigned int*>(sk);
+            unsigned int* hc = hk + kPenHashSlots;
+            for (int i = tid; i < kPenHashSlots; i += kGenThreads) {
+                hk[i] = kPenEmpty;
+                hc[i] = 0u;
+            }
+            __syncthreads();
+            for (long long j0 = 0; j0 < wlen; j0 += kGenThreads * kBatch) {
+                int t[kBatch];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    const long long j = j0 + q * kGenThreads + tid;
+                    t[q] = j < wlen ? a.hist[wstart + j] : -1;
+                }
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) {
+                    if (t[q] < 0 || t[q] >= V) continue;  // ids outside the vocabulary never match
+                    const unsigned key = static_cast<unsigned>(t[q]);
+                    unsigned h = (key * 2654435761u) >> (32 - kPenHashBits);
+                    for (int probe = 0; probe < kPenHashSlots; ++probe) {
+                        const unsigned prev = atomicCAS(hk + h, kPenEmpty, key);
+                        if (prev == kPenEmpty || prev == key) {
+                            atomicAdd(hc + h, 1u);
+                            break;
+                        }
+                        h = (h + 1u) & (kPenHashSlots - 1u);
+                    }
+                }
+            }
+            __syncthreads();
+            for (int i0 = 0; i0 < kPenHashSlots; i0 += kGenThreads * kBatch) {
+                unsigned key[kBatch];
+                float lv[kBatch];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) key[q] = hk[i0 + q * kGenThreads + tid];
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q) lv[q] = key[q] != kPenEmpty ? W[key[q]] : 0.0f;
+#pragma unroll
+                for (int q = 0; q < kBatch; ++q)
+                    if (key[q] != kPenEmpty)
+                        W[key[q]] = penalise(lv[q], hc[i0 + q * kGenThreads + tid], p.repeat_penalty,
+                                             p.frequency_penalty, p.presence_penalty);
+            }
+            __syncthreads();
+        } else if (wlen > 0) {  // history loads batched ahead of the atomics, as above
             for (long long j0 = 0; j0 < wlen; j0 += kGenThreads * kBatch) {
                 int t[kBatch];
 #pragma unroll
@@ -169,7 +213,7 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
             sh_u = u;
         }
         __syncthreads();
-        const int token = keep > 0 ? draw_row<kGenThreads>(K, fo, sh_u, fs, &sh_int[0]) : 0;
+        const int token = keep > 0 ? draw_row<kGenThreads>(K, fo, sh_u, fs, &sh_int[0], sk) : 0;
         if (a.out_probs != nullptr) {
             float* pr = a.out_probs + base;
             for (int i = tid; i < V; i += kGenThreads) pr[i] = 0.0f;

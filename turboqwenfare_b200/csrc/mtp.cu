@@ -53,24 +53,11 @@ __device__ __forceinline__ Workspace workspace(const MtpScratch& g, int cta) {
     return w;
 }
 
-// The row's logits into W, loads batched ahead of the stores (the compiler
-// cannot tell that W and the logits do not alias, so an unbatched loop pays
-// a full memory latency per element).
+// The row's logits into W (vector loads, batched ahead of the stores: the
+// compiler cannot tell that W and the logits do not alias).
 template <int DT>
 __device__ void load_row(const MtpArgs& m, const void* base, size_t row, float* W) {
-    for (int i0 = 0; i0 < m.vocab; i0 += kMT * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            const int i = i0 + q * kMT + threadIdx.x;
-            v[q] = i < m.vocab ? logit_at<DT>(base, row * m.ld, i) : 0.0f;
-        }
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            const int i = i0 + q * kMT + threadIdx.x;
-            if (i < m.vocab) W[i] = v[q];
-        }
-    }
+    load_row_to<DT, kMT>(base, row * m.ld, m.vocab, W);
     __syncthreads();
 }
 
@@ -192,7 +179,7 @@ __global__ void __launch_bounds__(kMT, 1) mtp_rows_kernel(MtpArgs m, MtpScratch 
         filter_row(A.W, A.E, A.K, m.vocab, p, red, &fo, fs, sk);
         if (tgt) {  // the sampler's draw with u_L: the bonus token, or the zero-residual fallback
             const float uL = m.uniforms[static_cast<size_t>(s) * T + L];
-            const int t = draw_row<kMT>(A.K, fo, uL, fs, &sh[0]);
+            const int t = draw_row<kMT>(A.K, fo, uL, fs, &sh[0], sk);
             if (threadIdx.x == 0) g.pick[static_cast<size_t>(sl) * T + j] = t;
         }
         if (!tgt || j < L) {
