@@ -364,6 +364,40 @@ int tqfs_mtp_commit(int rows, int draft_len, int cap, const int32_t* accepted_de
  */
 int tqfs_rng_draw(int rows, int count, uint64_t* rng_state_dev, float* out_dev, void* stream);
 
+/* ---- LM head on the tensor cores -------------------------------------- */
+/*
+ * logits = hidden . weight^T for a batch of rows: the producer step of the
+ * sampling path (`lm_head.matvec`, src/model/qwen36/weights.rs:400-410, one
+ * row at a time in f32 on the host in the reference). hidden_dev: rows x
+ * hidden bf16 (row stride ldx elements), weight_dev: vocab x hidden bf16
+ * (row stride ldw), both K-major; tcgen05 MMAs accumulate in f32 in tensor
+ * memory. hidden must be a multiple of 64; bases 16-byte aligned; ldx and ldw
+ * multiples of 8; logits_dev: rows x ld f32, ld >= vocab and a multiple of 4.
+ * err_dev: one int the kernel sets to 1 if a wait inside it ran out (2 s).
+ */
+int tqfs_lm_head_logits(const void* hidden_dev, const void* weight_dev, int rows, int hidden, int vocab,
+                        long long ldx, long long ldw, float* logits_dev, long long ld, int* err_dev,
+                        void* stream);
+/*
+ * The LM head fused with sampling: the logits of tqfs_lm_head_logits never
+ * leave the chip. The GEMM epilogue applies the row's penalties (the
+ * history window as tqfs_sample takes it) and keeps the row's top-k keys
+ * (ties by ascending id) over the tiles a CTA computes; one warp per row
+ * merges the CTAs' lists into the exact top-k and runs softmax, top_p, min_p
+ * and the draw exactly as tqfs_sample does, from uniforms_dev or the rows'
+ * xoshiro states. Served rows: greedy rows (the argmax, as
+ * top_logit_candidates) and rows with 0 < top_k <= 32 whose penalty window
+ * is at most 8192 tokens with at most 24 distinct ids in any 256 consecutive
+ * ids; other rows get TQFS_ROW_ERR_UNSUPPORTED and token -1 (sample them
+ * with tqfs_lm_head_logits and tqfs_sample), and a wait inside the GEMM that
+ * runs out (2 s) gives TQFS_ROW_ERR_TIMEOUT. Operand rules as
+ * tqfs_lm_head_logits.
+ */
+int tqfs_lm_head_sample(tqfs_handle* handle, const void* hidden_dev, const void* weight_dev, int rows,
+                        int hidden, int vocab, int64_t ldx, int64_t ldw, const int32_t* hist_dev,
+                        const int64_t* hist_off_dev, const tqfs_params* params_dev, const float* uniforms_dev,
+                        uint64_t* rng_state_dev, int32_t* out_token_dev, int32_t* out_status_dev, void* stream);
+
 /* ---- drop-in Sampler (host pointers; synchronising) ---------------------- */
 /*
  * `Sampler::new(&SamplingParams)` (src/sampling/mod.rs:45-53): greedy iff

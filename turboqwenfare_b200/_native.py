@@ -41,7 +41,7 @@ EXPORTS = [
     "tqfs_apply_penalties", "tqfs_mtp_verify", "tqfs_shard_record_words", "tqfs_shard_export",
     "tqfs_shard_merge", "tqfs_nccl_unique_id", "tqfs_nccl_comm_init", "tqfs_nccl_comm_init_timeout", "tqfs_nccl_comm_destroy",
     "tqfs_nccl_wait",
-    "tqfs_sample_vocab_sharded", "tqfs_sample_static", "tqfs_decode_begin", "tqfs_decode_append", "tqfs_mtp_commit", "tqfs_rng_draw", "tqfs_sampler_new", "tqfs_sampler_is_greedy", "tqfs_sampler_select", "tqfs_sampler_get_state",
+    "tqfs_sample_vocab_sharded", "tqfs_sample_static", "tqfs_decode_begin", "tqfs_decode_append", "tqfs_mtp_commit", "tqfs_rng_draw", "tqfs_lm_head_logits", "tqfs_lm_head_sample", "tqfs_sampler_new", "tqfs_sampler_is_greedy", "tqfs_sampler_select", "tqfs_sampler_get_state",
     "tqfs_sampler_free",
 ]
 
@@ -124,6 +124,8 @@ def lib() -> ctypes.CDLL:
     L.tqfs_decode_append.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
     L.tqfs_mtp_commit.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.tqfs_rng_draw.argtypes = [i32, i32, vp, vp, vp]
+    L.tqfs_lm_head_logits.argtypes = [vp, vp, i32, i32, i32, i64, i64, vp, i64, vp, vp]
+    L.tqfs_lm_head_sample.argtypes = [vp, vp, vp, i32, i32, i32, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp]
     L.tqfs_sampler_new.argtypes = [vp, ctypes.POINTER(Params), i32, u64, ctypes.POINTER(vp)]
     L.tqfs_sampler_is_greedy.argtypes = [vp]
     L.tqfs_sampler_select.argtypes = [vp, vp, i64, vp, i64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32)]

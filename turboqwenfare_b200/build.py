@@ -16,7 +16,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libtqfsample.so")
-SOURCES = ["api.cu", "stream.cu", "general.cu", "penalties.cu", "noalloc.cu", "mtp.cu", "decode.cu"]
+SOURCES = ["api.cu", "stream.cu", "general.cu", "penalties.cu", "noalloc.cu", "mtp.cu", "decode.cu", "lmhead.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -60,6 +60,7 @@ struct tqfs_handle {
     DeviceBuffer mtp;          // MTP verify workspaces
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
+    DeviceBuffer lm;           // fused LM-head per-row lists (zeroed per call)
     bool row_th_dirty = false; // a call's stream kernel failed to launch after its window pre-pass
     int stall_row_p1 = 0;      // test hook for the next call (tqfs_debug_stall_row)
     unsigned long long stall_wait_ns = 0;
@@ -434,6 +435,67 @@ int tqfs_sample(tqfs_handle* h, const void* logits_dev, int dtype, int rows, int
     a.out_status = out_status_dev;
     a.top4_only = 0;
     return run_sample(h, a, static_cast<cudaStream_t>(stream));
+}
+
+int tqfs_lm_head_sample(tqfs_handle* h, const void* hidden_dev, const void* weight_dev, int rows, int hidden,
+                        int vocab, int64_t ldx, int64_t ldw, const int32_t* hist_dev, const int64_t* hist_off_dev,
+                        const tqfs_params* params_dev, const float* uniforms_dev, uint64_t* rng_state_dev,
+                        int32_t* out_token_dev, int32_t* out_status_dev, void* stream) {
+    if (!h) return TQFS_ERR_INVALID_ARG;
+    if (rows < 0 || vocab < 0 || hidden <= 0 || hidden % 64 != 0)
+        return fail(h, TQFS_ERR_INVALID_ARG, "rows %d, vocab %d, hidden %d (a positive multiple of 64)", rows, vocab,
+                    hidden);
+    if (rows == 0) return TQFS_OK;
+    if (vocab == 0) return fail(h, TQFS_ERR_INVALID_ARG, "vocab is 0");
+    if (!hidden_dev || !weight_dev || !params_dev || !out_token_dev)
+        return fail(h, TQFS_ERR_INVALID_ARG, "hidden, weight, params and out_token are required");
+    if (!uniforms_dev && !rng_state_dev) return fail(h, TQFS_ERR_INVALID_ARG, "need uniforms or rng_state");
+    if (hist_off_dev && !hist_dev) return fail(h, TQFS_ERR_INVALID_ARG, "history is NULL");
+    if (ldx < hidden || ldw < hidden || (ldx * 2) % 16 != 0 || (ldw * 2) % 16 != 0 || !aligned16(hidden_dev) ||
+        !aligned16(weight_dev))
+        return fail(h, TQFS_ERR_INVALID_ARG, "hidden and weight need 16-byte aligned bases and row strides");
+    int st;
+    if ((st = ensure_current(h)) != TQFS_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const tqfs::Plan plan = tqfs::plan_stream(rows, vocab, TQFS_DTYPE_F32);
+    if (plan.chunks == 0) return fail(h, TQFS_ERR_UNSUPPORTED, "vocab %d too large", vocab);
+    tqfs::SampleArgs a{};
+    a.dtype = TQFS_DTYPE_F32;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.vocab_route = vocab;
+    a.ld = vocab;
+    a.hist = hist_dev;
+    a.hist_off = hist_off_dev;
+    a.params = params_dev;
+    if ((st = ensure_scratch(h, rows, plan, a, s)) != TQFS_OK) return st;
+    cudaError_t e = h->lm.reserve(tqfs::lmhead_state_bytes(rows));
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->lm.ptr, 0, tqfs::lmhead_state_bytes(rows), s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "LM-head state");
+    if (hist_off_dev) {
+        TimingScope ts(h, s, 2);
+        e = tqfs::launch_window(a, plan, s);
+        if (e != cudaSuccess) return cuda_fail(h, e, "window pre-pass launch");
+    }
+    tqfs::LmArgs m{};
+    m.rows = rows;
+    m.hidden = hidden;
+    m.vocab = vocab;
+    m.mode = tqfs::kLmSelect;
+    m.wait_ns = tqfs::kDefaultWaitNs;
+    m.params = params_dev;
+    m.hist_off = hist_off_dev;
+    m.win_off = hist_off_dev ? a.win_off : nullptr;
+    m.win_ent = hist_off_dev ? a.win_ent : nullptr;
+    m.chunks = plan.chunks;
+    m.chunk_len = plan.chunk_len;
+    tqfs::lmhead_state_layout(rows, h->lm.ptr, &m);
+    st = tqfs::launch_lmhead(hidden_dev, weight_dev, ldx, ldw, m, s);
+    if (st != TQFS_OK) return st == TQFS_ERR_CUDA ? cuda_fail(h, cudaGetLastError(), "LM-head launch")
+                                                  : fail(h, st, "LM-head tensor maps");
+    e = tqfs::launch_lmhead_finalize(m, uniforms_dev, rng_state_dev, out_token_dev, out_status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "LM-head finalize launch");
+    return TQFS_OK;
 }
 
 int tqfs_top_logit_candidates(tqfs_handle* h, const void* logits_dev, int dtype, int rows,

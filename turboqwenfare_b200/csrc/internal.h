@@ -124,6 +124,41 @@ size_t stream_scratch(int rows, const Plan& plan, void* base, SampleArgs* a);
 // The window pre-pass (a no-op without a history), then the stream kernel,
 // which also finalises its rows; after_window lets the stream kernel's
 // launch overlap the pre-pass.
+// ---- LM head (lmhead.cu) ----
+constexpr int kLmMaxK = 32;  // largest top_k the fused LM-head path serves
+enum : int { kLmDump = 0, kLmSelect = 1 };
+struct LmArgs {
+    int rows;
+    int hidden;
+    int vocab;
+    int mode;                        // kLmDump or kLmSelect
+    long long ld;                    // logits row stride (kLmDump)
+    float* logits;                   // kLmDump output
+    int* err;                        // set to 1 when a wait runs out
+    unsigned long long wait_ns;
+    // kLmSelect
+    const tqfs_params* params;
+    const int64_t* hist_off;         // null: no penalties
+    const uint32_t* win_off;         // stream-path window buckets (window_kernel)
+    const uint32_t* win_ent;
+    int chunks;
+    int chunk_len;
+    unsigned long long* bound;       // per row: the largest k-th key a CTA has published
+    int slots;                       // lists per row: the CTAs that share a row block
+    unsigned long long* top;         // rows x slots x kLmMaxK keys, each list sorted descending
+    uint32_t* cnt;                   // lists stored per row
+    uint32_t* flag;                  // per row: a list found no slot
+};
+// Per-row state of a kLmSelect call, zeroed before it: top | bound | cnt | flag | err.
+int lmhead_ctas_per_block(int rows);
+size_t lmhead_state_bytes(int rows);
+void lmhead_state_layout(int rows, void* base, LmArgs* a);
+// TQFS status: launches the GEMM (and its epilogue) for hidden x weight^T.
+int launch_lmhead(const void* hidden, const void* weight, long long ldx, long long ldw, const LmArgs& a,
+                  cudaStream_t s);
+cudaError_t launch_lmhead_finalize(const LmArgs& a, const float* uniforms, uint64_t* rng_state, int32_t* out_token,
+                                   int32_t* out_status, cudaStream_t s);
+
 cudaError_t launch_window(const SampleArgs& a, const Plan& plan, cudaStream_t s);
 cudaError_t launch_stream(const SampleArgs& a, const Plan& plan, cudaStream_t s, bool after_window);
 size_t general_scratch_bytes(int vocab, int ctas, size_t* stride, size_t* key_stride);
