@@ -373,7 +373,71 @@ def run_other_workloads(args, rank, world, local, h, stream, peak):
                  "whole_call_hbm_frac": round(alg / (ms / 10 / 1000.0) / 1e9 / peak, 4),
                  "algorithmic_bytes": alg, "l2": "inputs resident (136 MB, about L2 size), no flush",
                  "timing": stats}
+    del tgt, dft
+    out["lm_head"] = run_lm_head(args, rank, world, dev, h, stream)
     return out
+
+
+def run_lm_head(args, rank, world, dev, h, stream):
+    """The producer step on the tensor cores: logits = hidden . W^T for the
+    headline's 256 rows, hidden 2048 (the Qwen3.6 geometry of the reference,
+    src/model/qwen36/geometry.rs), V = 151,936, bf16 operands (random), f32
+    logits; alone (tqfs_lm_head_logits), feeding the sampler (then
+    tqfs_sample on c1x256's parameters and histories), and fused
+    (tqfs_lm_head_sample). The weights (622 MB) exceed L2, so every step
+    streams them from HBM."""
+    import torch
+    import turboqwenfare_b200._native as N
+    from turboqwenfare_b200 import workloads as W
+    from turboqwenfare_b200.sampler import params_tensor
+    rows, hidden, vocab = 256, 2048, 151_936
+    g = torch.Generator(device="cpu").manual_seed(args.seed + 31 * rank)
+    x = (torch.randn(rows, hidden, generator=g) * 0.5).to(torch.bfloat16).to(dev)
+    w = (torch.randn(vocab, hidden, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    b = W.config("c1x256", seed=args.seed + 7919 * rank)
+    hist = torch.from_numpy(b.hist).to(dev)
+    off = torch.from_numpy(b.hist_off).to(dev)
+    par = params_tensor(b.params, rows, dev)
+    uni = torch.from_numpy(b.uniforms).to(dev)
+    logits = torch.empty((rows, vocab), dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    tok = torch.empty(rows, dtype=torch.int32, device=dev)
+    sts = torch.empty(rows, dtype=torch.int32, device=dev)
+    L, s = N.lib(), stream.cuda_stream
+
+    def gemm(i):
+        h.check(L.tqfs_lm_head_logits(x.data_ptr(), w.data_ptr(), rows, hidden, vocab, hidden, hidden,
+                                      logits.data_ptr(), vocab, err.data_ptr(), s))
+
+    def gemm_sample(i):
+        gemm(i)
+        h.check(L.tqfs_sample(h.ptr, logits.data_ptr(), N.DTYPE_F32, rows, vocab, vocab, hist.data_ptr(),
+                              off.data_ptr(), par.data_ptr(), uni.data_ptr(), None, tok.data_ptr(), None, None,
+                              sts.data_ptr(), s))
+
+    def fused(i):
+        h.check(L.tqfs_lm_head_sample(h.ptr, x.data_ptr(), w.data_ptr(), rows, hidden, vocab, hidden, hidden,
+                                      hist.data_ptr(), off.data_ptr(), par.data_ptr(), uni.data_ptr(), None,
+                                      tok.data_ptr(), sts.data_ptr(), s))
+
+    flops = 2.0 * rows * hidden * vocab
+    peaks = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")))
+    res = {"rows_per_gpu": rows, "hidden": hidden, "vocab": vocab, "operands": "bf16 (random), f32 accumulate",
+           "algorithmic_flops": flops, "weight_bytes": vocab * hidden * 2}
+    for name, f in (("gemm", gemm), ("gemm_then_sample", gemm_sample), ("fused", fused)):
+        for i in range(3):
+            f(i)
+        ms, stats = timed_passes(f, 10, stream, world, min_s=0.2)
+        us = ms / 10 * 1000.0
+        res[name] = {"us_per_step": round(us, 1), "rows_per_s": round(rows * world / (us / 1e6), 1), "timing": stats}
+    tf = flops / (res["gemm"]["us_per_step"] / 1e6) / 1e12
+    res["gemm"]["tflops"] = round(tf, 1)
+    res["gemm"]["tensor_frac"] = round(tf / peaks["bf16_tflops"], 4)
+    res["gemm"]["weight_gbs"] = round(vocab * hidden * 2 / (res["gemm"]["us_per_step"] / 1e6) / 1e9, 1)
+    res["gemm"]["peak_source"] = "measured bf16_tflops (burst)"
+    res["err"] = int(err.item())
+    del w, logits
+    return res
 
 
 def run_ours(args):
