@@ -153,6 +153,7 @@ __device__ __forceinline__ int lm_row_k(const LmArgs& a, int row) {
 namespace {
 
 
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     lmhead_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                   LmArgs a) {
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = mb * kBM + quad * 32 + lane;
         int k = 0;
         tqfs_params p{};
-        if (a.mode == kLmSelect && row < a.rows) {
+        if (MODE == kLmSelect && row < a.rows) {
             k = lm_row_k(a, row);
             if (k != 0) p = a.params[row];
         }
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         unsigned long long lst[32];
 #pragma unroll
         for (int r = 0; r < 32; ++r) lst[r] = 0ull;
-        const bool sel = __any_sync(0xFFFFFFFFu, k != 0);
+        const bool sel = MODE == kLmSelect && __any_sync(0xFFFFFFFFu, k != 0);
         int* rk = lm_rk + (warp - kEpiThread0 / 32) * 32;  // the warp's rows' k
         rk[lane] = k;
         __syncwarp();
@@ -419,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                     }
                 }
-                if (a.mode == kLmDump && row < a.rows) {
+                if (MODE == kLmDump && row < a.rows) {
                     float* out = a.logits + static_cast<size_t>(row) * a.ld + col0 + c * 32;
                     const int lim = a.vocab - (col0 + c * 32);
                     if (lim >= 32) {
@@ -577,14 +578,17 @@ int launch_lmhead(const void* hidden, const void* weight, long long ldx, long lo
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        if (cudaFuncSetAttribute(lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(lmhead_kernel<kLmDump>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(lmhead_kernel<kLmSelect>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+                cudaSuccess)
             return TQFS_ERR_CUDA;
         configured = dev;
     }
     const int n_mb = (a.rows + kBM - 1) / kBM;
     const int grid = n_mb * lmhead_ctas_per_block(a.rows);
-    lmhead_kernel<<<grid, kThreads, kSmemBytes, s>>>(mx, mw, a);
+    if (a.mode == kLmSelect) lmhead_kernel<kLmSelect><<<grid, kThreads, kSmemBytes, s>>>(mx, mw, a);
+    else lmhead_kernel<kLmDump><<<grid, kThreads, kSmemBytes, s>>>(mx, mw, a);
     return cudaGetLastError() == cudaSuccess ? TQFS_OK : TQFS_ERR_CUDA;
 }
 
