@@ -13,7 +13,7 @@
 
 namespace tqfs {
 
-constexpr int kFilterThreads = 512;
+constexpr int kFilterThreads = 1024;
 
 __device__ __forceinline__ float block_max(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -287,26 +287,35 @@ __device__ __forceinline__ void chunk_summary(const float (&v)[kSumGroups], int 
                                               SumShared* sh, StageSlot* stage, int nslots) {
     const int lane = threadIdx.x & 31;
     const int e0 = binade_of(start * (1.0 - 1.0 / 64.0));
+    // Both bounds in binade e0: the chunk's partial sums all lie in e0, so
+    // binade e0 + 1 is never asked for (it is marked unusable; the walk
+    // checks the binade of s before it adds a chunk whole).
+    const bool two = binade_of((start + dsum) * (1.0 + 1.0 / 64.0)) != e0;
     unsigned r0 = 0u, r1 = 0u;  // below 2^22 units a term: the sums fit 32 bits
-    bool b0 = false, b1 = false;
+    bool b0 = false, b1 = !two;
     if (e0 >= kUnitsMinE) {
         const float sc0 = units_scale(e0), sc1 = units_scale(e0 + 1);
+        if (two) {
 #pragma unroll
-        for (int g = 0; g < kSumGroups; ++g) {
-            r0 += units_f32(v[g], sc0, b0);
-            r1 += units_f32(v[g], sc1, b1);
+            for (int g = 0; g < kSumGroups; ++g) {
+                r0 += units_f32(v[g], sc0, b0);
+                r1 += units_f32(v[g], sc1, b1);
+            }
+        } else {
+#pragma unroll
+            for (int g = 0; g < kSumGroups; ++g) r0 += units_f32(v[g], sc0, b0);
         }
     } else {
 #pragma unroll
         for (int g = 0; g < kSumGroups; ++g) {
             r0 += units_any(v[g], e0, b0);
-            r1 += units_any(v[g], e0 + 1, b1);
+            if (two) r1 += units_any(v[g], e0 + 1, b1);
         }
     }
     r0 = __reduce_add_sync(kFullMask, b0 ? 0u : r0);
     r1 = __reduce_add_sync(kFullMask, b1 ? 0u : r1);
     const unsigned okb = (__any_sync(kFullMask, b0) ? 0u : 1u) | (__any_sync(kFullMask, b1) ? 0u : 2u);
-    const bool suspect = okb != 3u || binade_of((start + dsum) * (1.0 + 1.0 / 64.0)) != e0;
+    const bool suspect = two || okb != 1u;
     int slot = -1;
     if (suspect && stage != nullptr) {
         if (lane == 0) slot = atomicAdd(&sh->nstage, 1);
@@ -556,6 +565,7 @@ constexpr int kMaxBig = 160;        // bins above kWarpSortMax (at most V / kWar
 // Bins of e below kBinCut (e < 2^-20, the largest e being 1) are counted as
 // one aggregate in bin 0; a prefix that reaches into them is the whole row.
 constexpr int kBinCut = 1712;       // the bin of 2^-20
+constexpr int kPBinMinShift = 8;    // the finest bins of p: 2^8 values each
 constexpr int kBinsHi = kBinsE - kBinCut;
 constexpr int kBinBytes = kFilterThreads / 32 * kBinsHi * 2;  // per-warp 16-bit counts of bins >= kBinCut
 constexpr int kStageSlots = (kSegCap * 8 - kBinBytes) / static_cast<int>(sizeof(StageSlot));
@@ -876,10 +886,17 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
     // has p >= P*, and an entry with p >= P* lies in an e bin >= lo - 1. Bins
     // of p are ranges of p, so sorting each bin's entries and concatenating
     // the bins from the top gives the (p desc, id asc) order.
+    // The bins of p are the values' leading bits above bit psh, counted from
+    // the bin of P*: psh is the smallest (finest) shift that fits the range
+    // [P*, p_max] in kBinsE bins (19, the e bins' width, always does).
     const float pstar = lo > 0 ? __fdiv_rn(bin_low_f(lo), total) : 0.0f;
     const float e_cut = bin_low_f(lo > 0 ? lo - 1 : 0);
-    const int pb_hi = static_cast<int>(__float_as_uint(pmax) >> 19);
-    const int pb_lo = static_cast<int>(__float_as_uint(pstar) >> 19);
+    const uint32_t pbits_hi = __float_as_uint(pmax), pbits_lo = __float_as_uint(pstar);
+    int psh = kPBinMinShift;
+    while (psh < 19 && (pbits_hi >> psh) - (pbits_lo >> psh) >= static_cast<uint32_t>(kBinsE)) ++psh;
+    const uint32_t pbase = pbits_lo >> psh;
+    const int pb_hi = static_cast<int>((pbits_hi >> psh) - pbase);
+    const int pb_lo = 0;
     unsigned int* pc = fs->cnt;  // entries per bin of p (the e bins are done)
     unsigned int* ps = fs->pstart;
     for (int b = tid; b < kBinsE; b += NT) pc[b] = 0u;
@@ -896,7 +913,11 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
             if (!(e >= e_cut)) return;
             const float pj = __fdiv_rn(e, total);
             if (!(pj >= pstar)) return;
-            const uint32_t pb = __float_as_uint(pj) >> 19;
+            const uint32_t pb = (__float_as_uint(pj) >> psh) - pbase;
+            if (pb >= static_cast<uint32_t>(kBinsE)) {  // p above p_max: not a row this path takes
+                fs->fail = 1;
+                return;
+            }
             if (pass == 0) {
                 atomicAdd(pc + pb, 1u);
             } else {
@@ -923,7 +944,7 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
             }
         }
         for (int j = 4 * v4 + tid; j < V; j += NT) visit(E[j], j);
-        __syncthreads();
+        if (__syncthreads_or(fs->fail)) return false;
         if (pass == 0) {  // bin starts, from the top bin down
             unsigned c = 0u;
             unsigned cb[kPerT];
