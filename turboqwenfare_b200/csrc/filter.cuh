@@ -160,6 +160,7 @@ namespace tqfs {
 // loops do (src/sampling/mod.rs:199-207, 236-245).
 constexpr int kSumChunk = 512;
 constexpr int kSumGroups = kSumChunk / 32;
+static_assert(kSumGroups <= 32, "a lane per group in the chunk walk");
 constexpr int kBatch = 8;  // loads a thread keeps in flight in a pass over a row
 constexpr int kSumMaxChunks = 512;  // n <= 262,144
 constexpr unsigned kFullMask = 0xFFFFFFFFu;
@@ -258,19 +259,28 @@ __device__ __forceinline__ unsigned units_any(float x, int e, bool& bad) {
     return static_cast<unsigned>(u);
 }
 
-// Adds the group's terms (lane j holds term g0 + j, j < gn) to s one by one,
-// in order, with the f32 add itself (every lane alike); stops (hit, pos =
-// 1-based position) at the first partial sum >= stop.
-static __device__ __noinline__ void walk_group(float v, int g0, int gn, float& s, float stop, int& pos,
-                                        bool& hit) {
+// Adds the group's terms (g32[0..gn), shared memory, 16-byte aligned; terms
+// g0 .. g0 + gn - 1) to s one by one, in order, with the f32 add itself
+// (every lane alike: the loads are broadcasts); stops (hit, pos = 1-based
+// position) at the first partial sum >= stop.
+static __device__ __noinline__ void walk_group(const float* g32, int g0, int gn, float& s, float stop,
+                                               int& pos, bool& hit) {
+    const float4* q = reinterpret_cast<const float4*>(g32);
+    float4 w[8];
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) w[j4] = q[j4];
     float acc = s;
     int at = -1;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const float x = __shfl_sync(kFullMask, v, j);
-        if (j < gn && at < 0) {
-            acc = __fadd_rn(acc, x);
-            if (acc >= stop) at = j;
+    for (int j4 = 0; j4 < 8; ++j4) {
+        const float xs[4] = {w[j4].x, w[j4].y, w[j4].z, w[j4].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int j = 4 * j4 + t;
+            if (j < gn && at < 0) {
+                acc = __fadd_rn(acc, xs[t]);
+                if (acc >= stop) at = j;
+            }
         }
     }
     s = acc;
@@ -348,12 +358,14 @@ __device__ __forceinline__ void chunk_summary(const float (&v)[kSumGroups], int 
     }
 }
 
-// The walk over chunk c, which the chunk step could not take whole, from s:
-// group by group, a group whole when its units in the binade of s are clean
-// (staged tables for binades elo and elo + 1, else computed for the binade
-// of s), else term by term. The terms come from the staging slot or are
-// copied to buf (kSumChunk floats of shared memory) first; the group loop is
-// not unrolled, which keeps the walking warp's code small.
+// The walk over chunk c, which the chunk step could not take whole, from s.
+// Lane j takes group g + j: its units in the binade e of s (staged tables for
+// binades elo and elo + 1, else computed for e) and whether they are clean;
+// the prefix of those units over the lanes adds every group up to the first
+// that is not clean, leaves binade e or reaches the stop value at once; that
+// group is added term by term, and the scan goes on from the group after it.
+// The terms come from the staging slot or are copied to buf (kSumChunk
+// floats of shared memory, 16-byte aligned) first.
 template <class Load>
 __device__ __noinline__ void walk_chunk(Load x, int n, int c, float stop, const SumShared* sh,
                                         const StageSlot* stage, float* buf, float& s, int& pos, bool& hit) {
@@ -372,37 +384,50 @@ __device__ __noinline__ void walk_chunk(Load x, int n, int c, float stop, const 
         vsrc = buf;
     }
     const int ng = (end - beg + 31) / 32;
+    int g = 0;
 #pragma unroll 1
-    for (int g = 0; g < ng && !hit; ++g) {
-        const float v = vsrc[g * 32 + lane];
+    while (g < ng && !hit) {
         const uint32_t gb = __float_as_uint(s) & 0x7FFFFFFFu;
         const uint32_t gbi = max(gb >> 23, 1u);
         const int e = static_cast<int>(gbi) - 127;
+        const int gj = g + lane;
         bool ok = false;
         unsigned units = 0u;
         if (st != nullptr) {
             const int gq = e - ebase;
-            if (gq >= 0 && gq < 2) {
-                ok = (st->gok >> (2 * g + gq)) & 1u;
-                units = st->gr[g][gq];
+            if (gj < ng && gq >= 0 && gq < 2) {
+                ok = (st->gok >> (2 * gj + gq)) & 1u;
+                units = st->gr[gj][gq];
             }
         } else {
-            bool bad = false;
-            const unsigned u = units_any(v, e, bad);
-            units = __reduce_add_sync(kFullMask, bad ? 0u : u);
-            ok = !__any_sync(kFullMask, bad);
-        }
-        if (ok) {
-            const unsigned long long nb = gb + static_cast<unsigned long long>(units);
-            if (nb < (static_cast<unsigned long long>(gbi + 1u) << 23)) {
-                const float t = __uint_as_float(static_cast<uint32_t>(nb));
-                if (!(t >= stop)) {
-                    s = t;
-                    continue;
+#pragma unroll 1
+            for (int h = g; h < ng; ++h) {
+                bool bad = false;
+                const unsigned u = units_any(vsrc[h * 32 + lane], e, bad);
+                const unsigned gs = __reduce_add_sync(kFullMask, bad ? 0u : u);
+                const bool gok = !__any_sync(kFullMask, bad);
+                if (lane == h - g) {
+                    units = gs;
+                    ok = gok;
                 }
             }
         }
-        walk_group(v, beg + g * 32, min(32, end - beg - g * 32), s, stop, pos, hit);
+        // below 2^22 units a term: a group's units fit 27 bits, the prefix 32
+        const unsigned long long pre = warp_incl_scan_u64(ok ? static_cast<unsigned long long>(units) : 0ull);
+        const unsigned long long nb = gb + pre;
+        const bool over = nb >= (static_cast<unsigned long long>(gbi + 1u) << 23);
+        const float t = __uint_as_float(static_cast<uint32_t>(nb));
+        const unsigned ev = __ballot_sync(kFullMask, gj < ng && (!ok || over || t >= stop));
+        if (ev == 0u) {
+            s = __shfl_sync(kFullMask, t, ng - g - 1);
+            break;
+        }
+        const int k = __ffs(ev) - 1;
+        const float before = __shfl_sync(kFullMask, t, k > 0 ? k - 1 : 0);
+        if (k > 0) s = before;
+        const int gw = g + k;
+        walk_group(vsrc + gw * 32, beg + gw * 32, min(32, end - beg - gw * 32), s, stop, pos, hit);
+        g = gw + 1;
     }
     __syncwarp();
 }
@@ -1048,7 +1073,8 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
 
 namespace tqfs {
 
-// W[0..V) holds the row's (penalised) logits. Leaves in K[0..keep) the kept
+// W[0..V) holds the row's (penalised) logits, 16-byte aligned; W is only
+// read. Leaves in K[0..keep) the kept
 // candidates as probability keys (order32(p) << 32 | ~token), sorted as the
 // reference sorts them (p descending, NaN last, id ascending), with keep and
 // the totals in *out. Steps:
@@ -1061,11 +1087,11 @@ namespace tqfs {
 //   the draw total (mod.rs:234).
 // With fs (and sk, kSegCap keys of shared memory) rows that qualify take
 // filter_row_fast, and the sequential sums of finite rows run as
-// exact_seq_prefix; without, every sum is one thread's loop. W is reused for
-// the candidates' tokens; E holds the exponentials; K needs pow2_at_least(V)
-// entries.
+// exact_seq_prefix; without, every sum is one thread's loop. `tokens` (V
+// words, may be W's own memory) receives the candidates' tokens; E holds the
+// exponentials; K needs pow2_at_least(V) entries.
 template <int NT = kFilterThreads>
-__device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
+__device__ void filter_row(const float* W, unsigned int* tokens, float* E, unsigned long long* K, int V,
                            const tqfs_params& p, float* red, FilterOut* out,
                            FastShared* fs = nullptr, unsigned long long* sk = nullptr) {
     if (fs != nullptr && filter_row_fast<NT>(W, E, K, V, p, red, out, fs, sk)) return;
@@ -1117,9 +1143,9 @@ __device__ void filter_row(float* W, float* E, unsigned long long* K, int V,
         total = out->total;
     }
     const int n2 = pow2_at_least(nc);
-    // Candidate tokens go to W (dead once E is computed) so that K can be
-    // rewritten with probability keys.
-    unsigned int* tokens = reinterpret_cast<unsigned int*>(W);
+    // Candidate tokens go to `tokens` (V words; W itself when W is the
+    // caller's copy, dead once E is computed) so that K can be rewritten with
+    // probability keys.
     for (int j = tid; j < nc; j += NT) tokens[j] = topk ? key_token(K[j]) : static_cast<uint32_t>(j);
     __syncthreads();
     for (int j = tid; j < n2; j += NT) {

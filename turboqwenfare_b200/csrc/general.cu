@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
             __syncthreads();
         }
         // ---- top_k, softmax, top_p, min_p (mod.rs:153-224) ---------------
-        filter_row(W, E, K, V, p, red, &fo, fs, sk);
+        filter_row(W, reinterpret_cast<unsigned int*>(W), E, K, V, p, red, &fo, fs, sk);
         // ---- draw (mod.rs:227-248) ----------------------------------------
         const int keep = fo.keep;
         if (tid == 0) {

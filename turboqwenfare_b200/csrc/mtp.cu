@@ -175,8 +175,16 @@ __global__ void __launch_bounds__(kMT, 1) mtp_rows_kernel(MtpArgs m, MtpScratch 
             continue;
         }
         const size_t row = tgt ? static_cast<size_t>(s) * T + j : static_cast<size_t>(s) * L + j;
-        load_row<DT>(m, tgt ? m.target : m.draft, row, A.W);
-        filter_row(A.W, A.E, A.K, m.vocab, p, red, &fo, fs, sk);
+        // An aligned f32 row is read where it lies (verification applies no
+        // penalties, so the values are the logits); anything else is widened
+        // or copied into W first.
+        const float* X = A.W;
+        if (DT == 0) {
+            const float* in = static_cast<const float*>(tgt ? m.target : m.draft) + row * m.ld;
+            if ((reinterpret_cast<uintptr_t>(in) & 15u) == 0u) X = in;
+        }
+        if (X == A.W) load_row<DT>(m, tgt ? m.target : m.draft, row, A.W);
+        filter_row(X, reinterpret_cast<unsigned int*>(A.W), A.E, A.K, m.vocab, p, red, &fo, fs, sk);
         if (tgt) {  // the sampler's draw with u_L: the bonus token, or the zero-residual fallback
             const float uL = m.uniforms[static_cast<size_t>(s) * T + L];
             const int t = draw_row<kMT>(A.K, fo, uL, fs, &sh[0], sk);

@@ -220,6 +220,13 @@ struct SL : StreamLayout<DT> {
 static_assert(SL<0>::kSmem <= 227 * 1024 - 512 && SL<1>::kSmem <= 227 * 1024 - 512, "stream smem");
 
 // max of three floats, NaN operands ignored (max.f32 with three inputs).
+// Lane-wise maximum of two pairs of bf16 values (PTX max.bf16x2).
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t x, uint32_t y) {
+    uint32_t r;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+    return r;
+}
+
 __device__ __forceinline__ float fmax3(float x, float y, float z) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(x), "f"(y), "f"(z));
@@ -610,15 +617,15 @@ __device__ __forceinline__ void slot_maxima(const void* vals, int n_here, int la
                 sm[j] = fmax3(fmaxf(v.x, v.y), v.z, v.w);
             }
         } else {
+            // Pairs of bf16 values maxed two at a time (max.bf16x2 returns the
+            // number when one side is NaN, as fmaxf does); the two halves
+            // left are widened exactly.
             const uint4* p = static_cast<const uint4*>(vals);
 #pragma unroll
             for (int j = 0; j < kSlots / 2; ++j) {
                 const uint4 u = p[j * 32 + lane];
-                const float a0 = fmaxf(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u));
-                const float a1 = fmaxf(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-                const float a2 = fmaxf(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u));
-                const float a3 = fmaxf(__uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
-                sm[j] = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+                const uint32_t m = bf16x2_max(bf16x2_max(u.x, u.y), bf16x2_max(u.z, u.w));
+                sm[j] = fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
             }
         }
     } else {
