@@ -176,6 +176,7 @@ struct StageSlot {
 
 struct SumShared {
     double d[kSumMaxChunks];          // chunk sums of the current round
+    double st[kSumMaxChunks];         // chunk starts (filter_row_fast's two-pass bulk phase)
     unsigned long long r[kSumMaxChunks][2];
     int elo[kSumMaxChunks];           // the chunk's first candidate binade
     unsigned char ok[kSumMaxChunks];  // bit q: binade elo + q usable (q < 2)
@@ -756,9 +757,12 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
         for (int j = 4 * v4 + tid; j < V; j += NT) lmax = fmaxf(lmax, W[j]);
     }
     const float mx = block_max(lmax, red);
-    // ---- one pass: e, the total's bulk phase, the bins of e ----------------
-    // Each warp takes one chunk a round; the next round's values are loaded
-    // while this round's are computed.
+    // ---- e and the bins of e, then the total's bulk phase -----------------
+    // Pass A: each warp takes one chunk a round (the next round's values are
+    // loaded while this round's are computed) and leaves E, the chunk's fp64
+    // sum and the bin counts; no barrier between rounds. The chunks' starts
+    // are then one block scan, and pass B (the bulk phase proper) reads each
+    // chunk back from E.
     unsigned int* hw = reinterpret_cast<unsigned int*>(sk);
     for (int i = tid; i < NW * kBinsHi / 2; i += NT) hw[i] = 0u;
     if (tid == 0) {
@@ -768,7 +772,6 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
     __syncthreads();
     unsigned int* my = hw + warp * (kBinsHi / 2);
     const int nch = (V + kSumChunk - 1) / kSumChunk;
-    double base = 0.0;
     bool bad = false;
     unsigned low = 0u;  // entries below kBinCut
     float wn[kSumGroups];
@@ -777,8 +780,7 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
         const int i = warp * kSumChunk + g * 32 + lane;
         wn[g] = i < V ? W[i] : 0.0f;
     }
-    for (int c0 = 0; c0 < nch; c0 += NW) {
-        const int c = c0 + warp;
+    for (int c = warp; c < nch; c += NW) {
         float v[kSumGroups];
 #pragma unroll
         for (int g = 0; g < kSumGroups; ++g) v[g] = wn[g];
@@ -791,47 +793,59 @@ __device__ bool filter_row_fast(const float* W, float* E, unsigned long long* K,
             }
         }
         double d = 0.0;
-        if (c < nch) {
 #pragma unroll
-            for (int g = 0; g < kSumGroups; ++g) {
-                const int i = c * kSumChunk + g * 32 + lane;
-                float e = 0.0f;
-                if (i < V) {
-                    e = exp_f32(__fdiv_rn(__fsub_rn(v[g], mx), p.temperature));
-                    E[i] = e;
-                    const uint32_t bin = __float_as_uint(e) >> 19;
-                    if (bin < static_cast<uint32_t>(kBinCut)) {
-                        ++low;
-                    } else if (bin < static_cast<uint32_t>(kBinsE)) {
-                        const uint32_t hb = bin - kBinCut;
-                        atomicAdd(my + (hb >> 1), 1u << ((hb & 1u) * 16u));
-                    } else {
-                        bad = true;  // above 2, infinite or NaN
-                    }
+        for (int g = 0; g < kSumGroups; ++g) {
+            const int i = c * kSumChunk + g * 32 + lane;
+            if (i < V) {
+                const float e = exp_f32(__fdiv_rn(__fsub_rn(v[g], mx), p.temperature));
+                E[i] = e;
+                const uint32_t bin = __float_as_uint(e) >> 19;
+                if (bin < static_cast<uint32_t>(kBinCut)) {
+                    ++low;
+                } else if (bin < static_cast<uint32_t>(kBinsE)) {
+                    const uint32_t hb = bin - kBinCut;
+                    atomicAdd(my + (hb >> 1), 1u << ((hb & 1u) * 16u));
+                } else {
+                    bad = true;  // above 2, infinite or NaN
                 }
-                v[g] = e;
                 d += static_cast<double>(e);
             }
-        } else {
-#pragma unroll
-            for (int g = 0; g < kSumGroups; ++g) v[g] = 0.0f;
         }
         d = warp_sum_f64(d);
-        if (lane == 0 && c < nch) sh->d[c] = d;
-        __syncthreads();
-        double st = base, rt = base;
-        for (int w = 0; w < NW && c0 + w < nch; ++w) {
-            const double dw = sh->d[c0 + w];
-            if (w < warp) st += dw;
-            rt += dw;
-        }
-        if (c < nch && !__any_sync(kFullMask, bad)) chunk_summary(v, c, st, d, sh, stage, kStageSlots);
-        base = rt;
+        if (lane == 0) sh->d[c] = d;
     }
     low = __reduce_add_sync(kFullMask, low);
     if (lane == 0) atomicAdd(&fs->low, low);
     if (__syncthreads_or(bad)) return false;
-    const double sum_e = base;
+    double sum_e;
+    {
+        static_assert(kSumMaxChunks <= NT, "a thread per chunk");
+        unsigned zc = 0u, tc;
+        double a = tid < nch ? sh->d[tid] : 0.0, zb = 0.0, tb;
+        block_scan3<NT>(zc, a, zb, tc, sum_e, tb, fs);
+        if (tid < nch) sh->st[tid] = a;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kSumGroups; ++g) {
+        const int i = warp * kSumChunk + g * 32 + lane;
+        wn[g] = i < V ? E[i] : 0.0f;
+    }
+    for (int c = warp; c < nch; c += NW) {
+        float v[kSumGroups];
+#pragma unroll
+        for (int g = 0; g < kSumGroups; ++g) v[g] = wn[g];
+        {
+            const int cn = c + NW;
+#pragma unroll
+            for (int g = 0; g < kSumGroups; ++g) {
+                const int i = cn * kSumChunk + g * 32 + lane;
+                wn[g] = (cn < nch && i < V) ? E[i] : 0.0f;
+            }
+        }
+        chunk_summary(v, c, sh->st[c], sh->d[c], sh, stage, kStageSlots);
+    }
+    __syncthreads();
     // ---- the total (warp 0) while the other warps merge the bin counts ----
     if (warp == 0) {
         float s = -0.0f;
