@@ -61,6 +61,7 @@ struct tqfs_handle {
     DeviceBuffer shard_send;   // this shard's records for the all-gather
     DeviceBuffer shard_recv;   // every shard's records
     DeviceBuffer lm;           // fused LM-head per-row lists (zeroed per call)
+    DeviceBuffer gen_hint;     // one word: general rows of the last sampling call
     bool row_th_dirty = false; // a call's stream kernel failed to launch after its window pre-pass
     int stall_row_p1 = 0;      // test hook for the next call (tqfs_debug_stall_row)
     unsigned long long stall_wait_ns = 0;
@@ -218,6 +219,14 @@ int run_sample(tqfs_handle* h, tqfs::SampleArgs& a, cudaStream_t s) {
     if (st != TQFS_OK) return st;
     const size_t esz = a.dtype == TQFS_DTYPE_F32 ? 4 : 2;
     a.vec_ok = aligned16(a.logits) && ((static_cast<size_t>(a.ld) * esz) % 16 == 0);
+    if (!a.top4_only) {
+        if (h->gen_hint.bytes == 0) {
+            cudaError_t e = h->gen_hint.reserve(sizeof(int));
+            if (e == cudaSuccess) e = cudaMemsetAsync(h->gen_hint.ptr, 0, sizeof(int), s);
+            if (e != cudaSuccess) return cuda_fail(h, e, "scratch allocation");
+        }
+        a.gen_hint = static_cast<int*>(h->gen_hint.ptr);
+    }
     cudaError_t e = launch_stream_path(h, a, plan, s, a.hist_off != nullptr && !a.top4_only);
     if (e != cudaSuccess) return cuda_fail(h, e, "stream kernel launch");
     if (a.top4_only) return TQFS_OK;

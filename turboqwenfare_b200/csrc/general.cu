@@ -228,6 +228,9 @@ __global__ void __launch_bounds__(kGenThreads, 1) general_kernel(SampleArgs a, G
     }
     __syncthreads();  // `list` is rewritten next round
     }
+    // The next call's stream kernel reads this count (it leaves SMs to
+    // general rows when there were some).
+    if (blockIdx.x == 0 && tid == 0 && a.gen_hint != nullptr) *a.gen_hint = carry;
 }
 
 }  // namespace

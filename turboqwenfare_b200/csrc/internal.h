@@ -52,6 +52,10 @@ struct SampleArgs {
     int vocab_offset;          // global id of this shard's first id
     unsigned long long* export_rec;  // rows x kShardRec: export mode (a shard)
     int top4_only;             // tqfs_top_logit_candidates: every row is greedy
+    // Device word: general rows of the handle's previous call (written by the
+    // general kernel, read by the stream kernel); null: the stream kernel
+    // keeps its whole grid.
+    int* gen_hint;
 };
 
 // Per-CTA working arrays of the general kernel (library scratch).

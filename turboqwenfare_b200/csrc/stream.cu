@@ -1163,6 +1163,17 @@ __device__ __forceinline__ void finalize_in_stream(const SampleArgs& a, int row,
                  (rw & kRowFailed) != 0ull, L, S, bins);
 }
 
+// A row the general kernel takes (the predicate that kernel applies).
+__device__ __forceinline__ bool general_row(const SampleArgs& a, int row) {
+    const tqfs_params p = a.params[row];
+    long long hs = 0, he = 0, ws, wl;
+    if (a.hist_off != nullptr) {
+        hs = a.hist_off[row];
+        he = a.hist_off[row + 1];
+    }
+    return row_mode(p, hs, he, a.hist_off != nullptr, a.vocab, false, &ws, &wl) == kModeGeneral;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a, int top4_diag) {
     constexpr int ES = Raw<DT>::kES;
@@ -1186,10 +1197,61 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
     }
     __syncwarp();
 
-    // The kernel behind this one (general rows, which read only the call's
-    // inputs) may launch now; its CTAs find room as this grid's CTAs exit.
+    // The previous call's count of general rows, read before the kernel
+    // behind this one (general rows, which read only the call's inputs and
+    // rewrite that count) may launch; its CTAs find room as this grid's CTAs
+    // exit.
+    const int hint = a.gen_hint != nullptr ? __ldcg(a.gen_hint) : 0;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int nw = static_cast<int>(gridDim.x) * kWarps;
+    // Warps are numbered across CTAs first, so consecutive units land on
+    // different SMs. The words of the warp's first position are loaded while
+    // the general rows are counted (below).
+    int grid = static_cast<int>(gridDim.x);
+    auto first_pos = [&](int g) {
+        const int gw = warp * g + static_cast<int>(blockIdx.x);
+        Pos f;
+        f.row = gw % a.rows;
+        f.u = gw / a.rows;
+        f.chunk = f.u * a.unit_len;
+        return f;
+    };
+    Pos pn = first_pos(grid);
+    unsigned long long w0 = info_word(a, pn, false, lane, false);
+    // With general rows in the call, the grid's last CTAs (one per general
+    // row, at most half the grid) leave at once, so that those rows start on
+    // their SMs now instead of when this grid ends, and the stream units
+    // spread over the CTAs that stay. The rows are counted when the previous
+    // call had general rows (a batch's mix changes slowly from step to step);
+    // every CTA reads the same hint and counts the same rows, so all agree
+    // on the split.
+    if (hint > 0) {
+        __shared__ int gen_rows;
+        if (threadIdx.x == 0) gen_rows = 0;
+        __syncthreads();
+        constexpr int kCountBatch = 4;
+        int c = 0;
+        for (int r0 = threadIdx.x; r0 < a.rows; r0 += blockDim.x * kCountBatch) {
+            bool gq[kCountBatch];
+#pragma unroll
+            for (int q = 0; q < kCountBatch; ++q) {
+                const int r = r0 + q * static_cast<int>(blockDim.x);
+                gq[q] = r < a.rows && general_row(a, r);
+            }
+#pragma unroll
+            for (int q = 0; q < kCountBatch; ++q) c += gq[q] ? 1 : 0;
+        }
+        c = __reduce_add_sync(0xFFFFFFFFu, c);
+        if (lane == 0 && c != 0) atomicAdd(&gen_rows, c);
+        __syncthreads();
+        if (gen_rows > 0) {
+            const int stay = grid - min(gen_rows, grid / 2);
+            if (static_cast<int>(blockIdx.x) >= stay) return;
+            grid = stay;
+            pn = first_pos(grid);
+            w0 = info_word(a, pn, false, lane, false);
+        }
+    }
+    const int nw = grid * kWarps;
     const int nw_row = nw % a.rows, nw_u = nw / a.rows;
     const unsigned long long budget = a.wait_ns != 0ull ? a.wait_ns : kDefaultWaitNs;
     const unsigned char* logits = static_cast<const unsigned char*>(a.logits);
@@ -1243,23 +1305,21 @@ __global__ void __launch_bounds__(SL<DT>::kBound, 1) stream_kernel(SampleArgs a,
             if (lane + 32 * m < ne) en[m] = __ldcg(src + lane + 32 * m);
     };
 
-    // Warps are numbered across CTAs first, so consecutive units land on
-    // different SMs. Prologue: the warp's first kNB positions q[0..kNB) are
-    // being copied into buffers 0..kNB-1; the words of position pn are in
-    // flight. q[i] sits in buffer (b + i) % kNB.
-    const int gw = warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
-    Pos pn;
-    pn.row = gw % a.rows;
-    pn.u = gw / a.rows;
-    pn.chunk = pn.u * a.unit_len;
+    // Prologue: the warp's first kNB positions q[0..kNB) are being copied
+    // into buffers 0..kNB-1; the words of position pn are in flight. q[i]
+    // sits in buffer (b + i) % kNB.
     Info q[kNB];
     {
         Info prev;
         prev.mode = -1;
 #pragma unroll
         for (int i = 0; i < kNB; ++i) {
-            if (i > 0) pn = next_pos(a, pn, nw_row, nw_u);
-            q[i] = decode(info_word(a, pn, same_unit(pn, prev), lane, false), pn, prev, a);
+            unsigned long long w = w0;
+            if (i > 0) {
+                pn = next_pos(a, pn, nw_row, nw_u);
+                w = info_word(a, pn, same_unit(pn, prev), lane, false);
+            }
+            q[i] = decode(w, pn, prev, a);
             prev = q[i];
         }
     }
