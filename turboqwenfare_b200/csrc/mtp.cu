@@ -100,43 +100,43 @@ __device__ __forceinline__ unsigned long long residual_units(const float* QT, co
 
 // The residual draw (see the file comment) over the dense q arrays. The
 // residuals are integers, so their prefix over ascending ids is exact in any
-// order: each thread sums a contiguous range of ids, a block scan gives the
-// ranges' offsets, and the thread whose range holds the first prefix above
-// thr walks it. Returns -1 (to every thread) when the residual mass is zero.
+// order: each warp sums a contiguous segment of ids (its lanes reading
+// consecutive ids), the warps' totals give the segments' offsets, and the
+// warp whose segment holds the first prefix above thr scans it 32 ids at a
+// time. Returns -1 (to every thread) when the residual mass is zero.
 __device__ int residual_token(const float* QT, const float* QD, int vocab, float u,
                               unsigned long long* wsum, int* shared_word) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = (vocab + kMT - 1) / kMT;
-    const int t0 = min(vocab, tid * per), t1 = min(vocab, t0 + per);
+    constexpr int NW = kMT / 32;
+    const int seg = (vocab + NW - 1) / NW;
+    const int s0 = min(vocab, warp * seg), s1 = min(vocab, s0 + seg);
     unsigned long long loc = 0ull;
-    for (int t = t0; t < t1; ++t) loc += residual_units(QT, QD, t);
-    unsigned long long inc = loc;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if (lane >= o) inc += y;
-    }
+#pragma unroll 8
+    for (int t = s0 + lane; t < s1; t += 32) loc += residual_units(QT, QD, t);
+    loc = warp_sum_u64(loc);
     if (threadIdx.x == 0) *shared_word = -1;
-    if (lane == 31) wsum[warp] = inc;
+    if (lane == 0) wsum[warp] = loc;
     __syncthreads();
     unsigned long long before = 0ull, total = 0ull;
-    for (int w = 0; w < kMT / 32; ++w) {
+    for (int w = 0; w < NW; ++w) {
         if (w < warp) before += wsum[w];
         total += wsum[w];
     }
-    const unsigned long long excl = before + inc - loc;
     if (total != 0ull) {
         const unsigned long long uq = static_cast<unsigned long long>(ldexp(static_cast<double>(u), 32));
         const unsigned long long lo = uq * total, hi = __umul64hi(uq, total);
         const unsigned long long thr = (hi << 32) | (lo >> 32);  // floor(uq * total / 2^32) < total
-        if (excl <= thr && thr < excl + loc) {
-            unsigned long long pre = excl;
-            for (int t = t0; t < t1; ++t) {
-                pre += residual_units(QT, QD, t);
-                if (pre > thr) {
-                    *shared_word = t;
+        if (before <= thr && thr < before + loc) {  // warp-uniform
+            unsigned long long pre = before;
+            for (int t0 = s0; t0 < s1; t0 += 32) {
+                const int t = t0 + lane;
+                const unsigned long long inc = pre + warp_incl_scan_u64(t < s1 ? residual_units(QT, QD, t) : 0ull);
+                const unsigned hit = __ballot_sync(0xFFFFFFFFu, t < s1 && inc > thr);
+                if (hit != 0u) {
+                    if (lane == __ffs(hit) - 1) *shared_word = t;
                     break;
                 }
+                pre = __shfl_sync(0xFFFFFFFFu, inc, 31);
             }
         }
     }
