@@ -101,9 +101,11 @@ __device__ __forceinline__ unsigned long long residual_units(const float* QT, co
 // The residual draw (see the file comment) over the dense q arrays. The
 // residuals are integers, so their prefix over ascending ids is exact in any
 // order: each warp sums a contiguous segment of ids (its lanes reading
-// consecutive ids), the warps' totals give the segments' offsets, and the
-// warp whose segment holds the first prefix above thr scans it 32 ids at a
-// time. Returns -1 (to every thread) when the residual mass is zero.
+// consecutive ids), the warps' totals give the segments' offsets; the segment
+// that holds the first prefix above thr is then split over every thread, a
+// block scan gives the pieces' offsets, and the thread whose piece holds it
+// walks its few ids. Returns -1 (to every thread) when the residual mass is
+// zero.
 __device__ int residual_token(const float* QT, const float* QD, int vocab, float u,
                               unsigned long long* wsum, int* shared_word) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -117,26 +119,34 @@ __device__ int residual_token(const float* QT, const float* QD, int vocab, float
     if (threadIdx.x == 0) *shared_word = -1;
     if (lane == 0) wsum[warp] = loc;
     __syncthreads();
-    unsigned long long before = 0ull, total = 0ull;
-    for (int w = 0; w < NW; ++w) {
-        if (w < warp) before += wsum[w];
-        total += wsum[w];
+    unsigned long long total = 0ull, cbefore = 0ull;
+    int cw = -1;
+    const unsigned long long uq = static_cast<unsigned long long>(ldexp(static_cast<double>(u), 32));
+    for (int w = 0; w < NW; ++w) total += wsum[w];
+    const unsigned long long lo = uq * total, hi = __umul64hi(uq, total);
+    const unsigned long long thr = (hi << 32) | (lo >> 32);  // floor(uq * total / 2^32) < total
+    for (int w = 0; w < NW && cw < 0; ++w) {
+        if (thr < cbefore + wsum[w]) cw = w;
+        else cbefore += wsum[w];
     }
-    if (total != 0ull) {
-        const unsigned long long uq = static_cast<unsigned long long>(ldexp(static_cast<double>(u), 32));
-        const unsigned long long lo = uq * total, hi = __umul64hi(uq, total);
-        const unsigned long long thr = (hi << 32) | (lo >> 32);  // floor(uq * total / 2^32) < total
-        if (before <= thr && thr < before + loc) {  // warp-uniform
-            unsigned long long pre = before;
-            for (int t0 = s0; t0 < s1; t0 += 32) {
-                const int t = t0 + lane;
-                const unsigned long long inc = pre + warp_incl_scan_u64(t < s1 ? residual_units(QT, QD, t) : 0ull);
-                const unsigned hit = __ballot_sync(0xFFFFFFFFu, t < s1 && inc > thr);
-                if (hit != 0u) {
-                    if (lane == __ffs(hit) - 1) *shared_word = t;
-                    break;
-                }
-                pre = __shfl_sync(0xFFFFFFFFu, inc, 31);
+    __syncthreads();  // wsum is reused below
+    if (total == 0ull) return -1;
+    const int c0 = min(vocab, cw * seg), c1 = min(vocab, c0 + seg);
+    const int per = (c1 - c0 + kMT - 1) / kMT;
+    const int t0 = min(c1, c0 + tid * per), t1 = min(c1, t0 + per);
+    unsigned long long piece = 0ull;
+    for (int t = t0; t < t1; ++t) piece += residual_units(QT, QD, t);
+    const unsigned long long inc = warp_incl_scan_u64(piece);
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    unsigned long long pre = cbefore + inc - piece;
+    for (int w = 0; w < warp; ++w) pre += wsum[w];
+    if (pre <= thr && thr < pre + piece) {
+        for (int t = t0; t < t1; ++t) {
+            pre += residual_units(QT, QD, t);
+            if (pre > thr) {
+                *shared_word = t;
+                break;
             }
         }
     }
