@@ -695,7 +695,13 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
         for (int j = 0; j < kSlots; ++j) g[j & 3] = fmaxf(g[j & 3], sm[j]);
         const float lane_max = fmaxf(fmaxf(g[0], g[1]), fmaxf(g[2], g[3]));
         if (k <= 32) {
-            thr = warp_rank_value(lane_max, k - 1, lane);
+            // the larger of two bounds each of which k values reach: the
+            // k-th lane maximum, and the lower of the two halves' ceil(k/2)-th
+            // (the first is weak for k near 32)
+            const int r2 = (k + 1) / 2 - 1;
+            thr = fmaxf(warp_rank_value(lane_max, k - 1, lane),
+                        fminf(warp_rank_value(fmaxf(g[0], g[2]), r2, lane),
+                              warp_rank_value(fmaxf(g[1], g[3]), r2, lane)));
         } else if (k <= 64) {
             const int r = (k + 1) / 2 - 1;
             thr = fminf(warp_rank_value(fmaxf(g[0], g[2]), r, lane),
