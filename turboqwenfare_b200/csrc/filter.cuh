@@ -1,8 +1,9 @@
 // The reference's filter chain for one row, run by one CTA of kFilterThreads
 // threads over working arrays in global memory (src/sampling/mod.rs:90-248).
 // Shared by the general kernel (rows the stream path does not own) and the
-// MTP verify kernel. Exact: candidates in the reference's order, the
-// sequential f32 sums done in that order by one thread.
+// MTP verify kernel. Exact: candidates in the reference's order, and the
+// results of the reference's sequential f32 sums in that order (reproduced
+// in parallel below, or by one thread's loop where a row does not qualify).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -564,11 +565,11 @@ __device__ __forceinline__ float exact_seq_sum(const float* x, int n, SumShared*
 //
 // Rows without a top_k cut whose top_p or min_p cuts the sorted probabilities
 // keep a prefix of the (p desc, id asc) order, so only a prefix that holds
-// the cut needs sorting. One fused pass computes the exponentials e, the
-// bulk phase of their sequential total, and a histogram of e by its 11
-// leading bits (exponent and 4 mantissa bits: bins are value ranges, and
-// since p = fl(e / total) is monotone in e, descending bins are descending p,
-// up to ties of p across a bin edge). After the total, with p bounds per bin
+// the cut needs sorting. A first pass computes the exponentials e, the
+// chunks' fp64 sums and a histogram of e by its 11 leading bits (exponent and
+// 4 mantissa bits: bins are value ranges, and since p = fl(e / total) is
+// monotone in e, descending bins are descending p, up to ties of p across a
+// bin edge); a second pass the bulk phase of their sequential total. After the total, with p bounds per bin
 // (e range / total, widened by 2^-23), the prefix is every bin down to
 //   min_p: the bin of the smallest e whose p can reach min_p * p_max;
 //   top_p: the first bin where a lower bound M of the mass of the bins

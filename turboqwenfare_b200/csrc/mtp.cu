@@ -19,7 +19,7 @@
 // an active penalty gets status TQFS_ROW_ERR_UNSUPPORTED.
 //
 // Two kernels per batch of sequences. mtp_rows_kernel runs every row at once
-// (one 512-thread CTA per row, persistent over the rows): the exact filter
+// (one CTA of kFilterThreads threads per row, persistent over the rows): the exact filter
 // chain of filter.cuh on each target and draft row, leaving per row the dense
 // q (every id's post-filter probability) and, for target rows, the sampler's
 // draw with u_L (greedy sequences: the target rows' argmax instead).
