@@ -159,6 +159,13 @@ float tqfs_xoshiro_next_f32(uint64_t state[4]);
  *                   (0 where filtered out), or NULL. Debug output.
  *   out_status_dev  rows int32 tqfs_row_status, or NULL
  *   stream          cudaStream_t (NULL = legacy default stream)
+ *
+ * Scheduling: rows without a small top_k cut (full-vocabulary rows) run on
+ * one SM each. When the handle's previous call had such rows, this call
+ * counts them first and keeps that many SMs free of the other rows' work so
+ * that they start at once; a batch's first call with such rows after one
+ * without runs them behind the other rows instead. Only the timing depends
+ * on this, never the results.
  */
 int tqfs_sample(tqfs_handle* handle, const void* logits_dev, int dtype, int rows,
                 int vocab, int64_t ld, const int32_t* hist_dev,
