@@ -703,9 +703,13 @@ __device__ __forceinline__ int unit_chunk(const void* vals, int n_here, bool sel
                         fminf(warp_rank_value(fmaxf(g[0], g[2]), r2, lane),
                               warp_rank_value(fmaxf(g[1], g[3]), r2, lane)));
         } else if (k <= 64) {
-            const int r = (k + 1) / 2 - 1;
-            thr = fminf(warp_rank_value(fmaxf(g[0], g[2]), r, lane),
-                        warp_rank_value(fmaxf(g[1], g[3]), r, lane));
+            // the larger of the halves' and the quarters' bounds (the halves'
+            // is weak for k near 64)
+            const int r = (k + 1) / 2 - 1, r4 = (k + 3) / 4 - 1;
+            thr = fmaxf(fminf(warp_rank_value(fmaxf(g[0], g[2]), r, lane),
+                              warp_rank_value(fmaxf(g[1], g[3]), r, lane)),
+                        fminf(fminf(warp_rank_value(g[0], r4, lane), warp_rank_value(g[1], r4, lane)),
+                              fminf(warp_rank_value(g[2], r4, lane), warp_rank_value(g[3], r4, lane))));
         } else {
             const int r = (k + 3) / 4 - 1;
             thr = fminf(fminf(warp_rank_value(g[0], r, lane), warp_rank_value(g[1], r, lane)),
